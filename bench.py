@@ -1,0 +1,441 @@
+"""Benchmark of the aggregated small-op path (the driver's contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--mode persistent|stream] [--workload mixed_24op]
+
+One step = the whole 16,384-request mixed stream (24 operators, fp32, sizes
+log-uniform in [256, 32768], seed 0) submitted through the reference-facing
+Python API (gpuos_ext.submit_* / submit_unary / submit_binary, one call per
+request) and flushed every 512 requests, ending with flush(sync=True).
+
+Printed (rank 0, one JSON line):
+  value      requests/s of the whole job with inputs resident in HBM, timed
+             with CUDA events on the submitting stream, max over ranks
+  e2e        the same with host buffers: pinned host -> device copy of every
+             input and device -> host copy of every output inside each step
+  roofline   the batch kernel (stream mode) timed per launch with CUDA events
+             around each launch: algorithmic bytes / launch time vs the
+             measured HBM copy bandwidth
+  cpu_baseline   the CPU oracle (a C port of the reference algorithm) on all
+             host cores, same stream
+  flush_p50_us   latency of a one-request flush(sync=True) and of a 1024 x 4096
+             add/mul flush, median of repeats
+With --impl reference the same stream runs on the CPU restatement of the
+reference's algorithm (the reference has no CPU path of its own; its GPU path
+is not a library this harness can drive safely).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HBM_FALLBACK_GBS = 6650.0
+L2_BYTES = 126 * 2 ** 20
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def allmax(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+def make_stream(name):
+    from gpuos_b200 import workloads as W
+    return W.STREAMS[name]()
+
+
+def run_step(ext, calls, flush_every):
+    for i, (fn, a) in enumerate(calls):
+        fn(*a)
+        if (i + 1) % flush_every == 0:
+            ext.flush(sync=False)
+    ext.flush(sync=True)
+
+
+def cpu_baseline(stream, min_seconds=5.0):
+    """The CPU port of the reference algorithm on every host core."""
+    import oracle
+    out = torch.empty(stream.out_bytes, dtype=torch.uint8)
+    items = [(0 if r.kind == "ew" else 1, r.op, r.p0, r.p1, r.a.view(stream.host_in),
+              r.b.view(stream.host_in) if r.b is not None else None, r.out.view(out),
+              list(r.axes), r.keepdim) for r in stream.requests]
+    reqs = oracle.make_reqs(items)
+    cores = os.cpu_count() or 1
+    oracle.run(reqs, cores)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        used = oracle.run(reqs, cores)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return {"value": reps * len(stream.requests) / el, "unit": "requests/s", "cores": used,
+            "kind": "port",
+            "sample": f"{reps} full passes of the {len(stream.requests)}-request stream "
+                      f"({el:.1f} s wall, liboracle.so on {used} threads)"}
+
+
+def flush_latency(ext, dev, reps=400):
+    """p50 of flush(sync=True) for one 4096-element add, and for the
+    1024 x 4096 add/mul batch."""
+    from gpuos_b200 import workloads as W
+    a = torch.randn(4096, device=dev)
+    b = torch.randn(4096, device=dev)
+    o = torch.empty(4096, device=dev)
+    single = []
+    for i in range(reps):
+        t0 = time.perf_counter()
+        ext.submit_add(a, b, o)
+        ext.flush(sync=True)
+        single.append(time.perf_counter() - t0)
+    st = W.micro_add_mul()
+    # four buffer sets so that L2 (126 MB) does not hold a set between repeats
+    sets = []
+    for _ in range(4):
+        din, dout = st.device_buffers(dev)
+        sets.append((din, dout, W.Submitter(ext).prepare(st, st.views(din, dout))))
+    micro = []
+    for i in range(60):
+        calls = sets[i % 4][2]
+        t0 = time.perf_counter()
+        for fn, args in calls:
+            fn(*args)
+        ext.flush(sync=True)
+        micro.append(time.perf_counter() - t0)
+    single.sort()
+    micro.sort()
+    return {"single_4096_add_us": round(single[len(single) // 2] * 1e6, 2),
+            "single_p99_us": round(single[int(len(single) * 0.99)] * 1e6, 2),
+            "micro_add_mul_1024x4096_us": round(micro[len(micro) // 2] * 1e6, 2)}
+
+
+def roofline_leg(stream, dev, steps, peak_gbs, peak_kind):
+    """Per-launch CUDA-event timing of the batch kernel (stream mode)."""
+    import gpuos_b200
+    import gpuos_b200.cabi as C
+    from gpuos_b200 import workloads as W
+    ex = C.Executor(torch.cuda.current_device(), mode=C.MODE_STREAM)
+    try:
+        din, dout = stream.device_buffers(dev)
+        views = stream.views(din, dout)
+        # the same routing as the Python API, bound to this executor
+        sub = W.Submitter(_CabiExt(ex))
+        calls = sub.prepare(stream, views)
+        fe = stream.flush_every
+        batch_bytes = []
+        for i in range(0, len(stream.requests), fe):
+            batch_bytes.append(sum(r.algo_bytes for r in stream.requests[i:i + fe]))
+        cs = torch.cuda.current_stream().cuda_stream
+        ex.set_timing(True)
+        for s in range(steps + 1):
+            if s == 1:
+                ex.take_timings()
+            for i, (fn, a) in enumerate(calls):
+                fn(*a)
+                if (i + 1) % fe == 0:
+                    ex.flush(sync=False, stream=cs)
+            ex.flush(sync=True, stream=cs)
+        ms = ex.take_timings()
+        per = len(batch_bytes)
+        assert len(ms) == steps * per, (len(ms), steps, per)
+        tot_bytes = sum(batch_bytes) * steps
+        tot_s = sum(ms) / 1e3
+        achieved = tot_bytes / tot_s / 1e9
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs,
+                "unit": "GB/s", "frac": round(achieved / peak_gbs, 4), "peak_kind": peak_kind,
+                "kernel": "gpuos_batch_kernel",
+                "avg_launch_us": round(sum(ms) / len(ms) * 1e3, 2),
+                "bytes_per_launch": int(sum(batch_bytes) / per),
+                "launches": len(ms), "traffic": None}
+    finally:
+        ex.close()
+
+
+class _CabiExt:
+    """gpuos_ext-shaped adapter over a cabi.Executor (used by the roofline leg)."""
+
+    def __init__(self, ex):
+        import gpuos_b200.cabi as C
+        self.ex, self.C = ex, C
+        ops = {"add": C.OP_ADD, "sub": C.OP_SUB, "mul": C.OP_MUL, "div": C.OP_DIV}
+        for k, v in ops.items():
+            setattr(self, f"submit_{k}", (lambda op: lambda a, b, o: ex.builtin(op, a, b, o))(v))
+        self.submit_unary = ex.unary
+        self.submit_binary = ex.binary
+        self.register_elementwise = ex.register_elementwise
+        self.register_reduce = ex.register_reduce
+        self.submit_reduce = ex.reduce
+
+
+# ---------------------------------------------------------------------------
+def bench_ours(args, world, rank, local):
+    import gpuos_b200
+    dev = torch.device("cuda", local)
+    ext = gpuos_b200.load()
+    stream = make_stream(args.workload)
+    n_req = len(stream.requests)
+    ext.init(8192, 256, mode=args.mode)
+    from gpuos_b200 import workloads as W
+    din, dout = stream.device_buffers(dev)
+    calls = W.Submitter(ext).prepare(stream, stream.views(din, dout))
+    fe = stream.flush_every
+
+    for _ in range(args.warmup):
+        run_step(ext, calls, fe)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    cur = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur.synchronize()
+    ev0.record(cur)
+    t0 = time.perf_counter()
+    q0 = ext.peek_queue()
+    for _ in range(args.steps):
+        run_step(ext, calls, fe)
+    ev1.record(cur)
+    ev1.synchronize()
+    wall = time.perf_counter() - t0
+    q1 = ext.peek_queue()
+    ev_s = ev0.elapsed_time(ev1) / 1e3
+    t_step = allmax(max(ev_s, wall) / args.steps, world)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    batches = q1["tail"] - q0["tail"]
+    launches = batches if args.mode == "stream" else max(1, q1["relaunches"] - q0["relaunches"])
+    # outputs of the last step are checked against the oracle on a sample
+    value = world * n_req / t_step
+
+    # e2e: host buffers, H2D of the inputs and D2H of the outputs every step
+    host_in = stream.host_in.pin_memory()
+    host_out = torch.empty(stream.out_bytes, dtype=torch.uint8).pin_memory()
+    for _ in range(2):
+        din.copy_(host_in, non_blocking=True)
+        run_step(ext, calls, fe)
+        host_out.copy_(dout, non_blocking=True)
+        cur.synchronize()
+    barrier(world)
+    ev0.record(cur)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        din.copy_(host_in, non_blocking=True)
+        run_step(ext, calls, fe)
+        host_out.copy_(dout, non_blocking=True)
+    ev1.record(cur)
+    ev1.synchronize()
+    wall_e2e = time.perf_counter() - t0
+    t_e2e = allmax(max(ev0.elapsed_time(ev1) / 1e3, wall_e2e) / args.steps, world)
+
+    lat = flush_latency(ext, dev) if rank == 0 else None
+    ext.shutdown()
+
+    peak, peak_kind = peaks()
+    roof = roofline_leg(stream, dev, max(2, min(args.steps, 5)), peak, peak_kind)
+    traffic = ROOT / "profiles" / "traffic.json"
+    if traffic.exists():
+        try:
+            tr = json.loads(traffic.read_text())
+            roof["traffic"] = tr.get(args.workload)
+        except (ValueError, OSError):
+            pass
+
+    if rank != 0:
+        return None
+    cpu = cpu_baseline(stream) if world == 1 else None
+    return {
+        "metric": "micro-ops/sec (requests/s) of the 16K mixed-op request stream",
+        "value": round(value, 1),
+        "unit": "requests/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_step * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seed 0)",
+        "config": {"workload": f"{args.workload}: {n_req} requests, 24 ops, fp32, sizes "
+                               "log-uniform [256, 32768], flush every 512",
+                   "mode": args.mode, "api": "gpuos_ext.submit_* per request",
+                   "l2": f"inputs {stream.in_bytes / 1e9:.2f} GB per step > 126 MB L2",
+                   "parallelism": f"{world} independent executors (one per GPU)"},
+        "gbs_whole_step": round(world * stream.algo_bytes / t_step / 1e9, 1),
+        "e2e": {"value": round(world * n_req / t_e2e, 1), "unit": "requests/s",
+                "h2d_bytes_per_step": stream.in_bytes, "d2h_bytes_per_step": stream.out_bytes},
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "flush_p50_us": lat,
+        "gpu_launches": int(launches * world),
+        "clocks": clk,
+    }
+
+
+def bench_reference(args, world, rank):
+    """The reference arm: the CPU restatement of the reference algorithm on
+    every host core, same stream, same metric."""
+    if rank != 0:
+        return None
+    import oracle
+    stream = make_stream(args.workload)
+    out = torch.empty(stream.out_bytes, dtype=torch.uint8)
+    items = [(0 if r.kind == "ew" else 1, r.op, r.p0, r.p1, r.a.view(stream.host_in),
+              r.b.view(stream.host_in) if r.b is not None else None, r.out.view(out),
+              list(r.axes), r.keepdim) for r in stream.requests]
+    reqs = oracle.make_reqs(items)
+    cores = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        oracle.run(reqs, cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        used = oracle.run(reqs, cores)
+    el = time.perf_counter() - t0
+    v = len(stream.requests) * args.steps / el
+    return {
+        "impl": "reference",
+        "metric": "micro-ops/sec (requests/s) of the 16K mixed-op request stream",
+        "value": round(v, 1), "unit": "requests/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seed 0)",
+        "config": {"workload": f"{args.workload}: {len(stream.requests)} requests",
+                   "engine": "liboracle.so (C port of the reference algorithm), all host cores"},
+        "cpu_baseline": {"value": round(v, 1), "unit": "requests/s", "cores": used, "kind": "port",
+                         "sample": f"the whole stream, {args.steps} steps"},
+        "e2e": {"value": round(v, 1), "unit": "requests/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default=os.environ.get("GPUOS_MODE", "persistent"),
+                    choices=["persistent", "stream"])
+    ap.add_argument("--workload", default="mixed_24op")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = (1, 0, 0) if args.impl == "reference" and "WORLD_SIZE" not in os.environ \
+        else (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+              int(os.environ.get("LOCAL_RANK", "0")))
+    if args.impl == "reference":
+        res = bench_reference(args, world, rank)
+    else:
+        world, rank, local = dist_setup(args.gpus)
+        res = bench_ours(args, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+// Builtin micro-op expressions, dtype load/store and 8-wide vector helpers.
+//
+// Every builtin elementwise op is the fp32 expression the reference evaluates
+// for it, written with the same operators in the same order, so that the
+// compiler's default contraction of a*b+c into fma (on in both nvcc and
+// NVRTC, which the reference uses without flags) gives the same rounding:
+//   add/mul/sub and the B==0 division rule: op_batch,
+//     src/persistent_kernel.cu:101-106
+//   the other ops: the expression strings of pytorch_ext/scheduler.py:145-153,
+//     192-205, 244-290, with the literal parameters replaced by p0/p1.
+// Loads widen fp16/bf16 exactly; stores round to nearest even
+// (ld_as_float / st_from_float, src/persistent_kernel.cu:60-78).
+#pragma once
+#include "gpuos_abi.h"
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+namespace gpuos {
+
+template <int V>
+__device__ __forceinline__ float op1(float A, float B, float p0, float p1) {
+  if constexpr (V == V_ADD) return A + B;
+  else if constexpr (V == V_MUL) return A * B;
+  else if constexpr (V == V_SUB) return A - B;
+  else if constexpr (V == V_DIV0) return (B != 0.f) ? (A / B) : 0.f;
+  else if constexpr (V == V_DIV) return (A / B);
+  else if constexpr (V == V_MAX) return (A > B ? A : B);
+  else if constexpr (V == V_MIN) return (A < B ? A : B);
+  else if constexpr (V == V_POW) return powf(A, B);
+  else if constexpr (V == V_RELU) return (A > 0.f ? A : 0.f);
+  else if constexpr (V == V_SIGMOID) return 1.f / (1.f + expf(-A));
+  else if constexpr (V == V_TANH) return tanhf(A);
+  else if constexpr (V == V_EXP) return expf(A);
+  else if constexpr (V == V_LOG) return logf(A);
+  else if constexpr (V == V_SQRT) return sqrtf(A);
+  else if constexpr (V == V_ABS) return fabsf(A);
+  else if constexpr (V == V_HARDSIGMOID) return fminf(fmaxf(0.2f * A + 0.5f, 0.f), 1.f);
+  else if constexpr (V == V_HARDSWISH) return A * fminf(fmaxf(A / 6.f + 0.5f, 0.f), 1.f);
+  else if constexpr (V == V_GELU)
+    return 0.5f * A * (1.f + tanhf(0.79788456f * (A + 0.044715f * A * A * A)));
+  else if constexpr (V == V_SIN) return sinf(A);
+  else if constexpr (V == V_COS) return cosf(A);
+  else if constexpr (V == V_LEAKY_RELU) return (A >= 0.f ? A : p0 * A);
+  else if constexpr (V == V_CLAMP) return fminf(fmaxf(A, p0), p1);
+  else if constexpr (V == V_ELU) return (A > 0.f ? A : p0 * (expf(A) - 1.f));
+  else if constexpr (V == V_SOFTPLUS) return (log1pf(expf(p0 * A)) / p0);
+  else if constexpr (V == V_CLAMP_MIN) return fmaxf(A, p0);
+  else if constexpr (V == V_CLAMP_MAX) return fminf(A, p0);
+  else return A;  // V_COPY
+}
+
+template <int V>
+__device__ __forceinline__ void op8(const float* A, const float* B, float* R, float p0, float p1) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) R[k] = op1<V>(A[k], B[k], p0, p1);
+}
+
+// Custom (NVRTC) expressions are spliced in here by the JIT executor source.
+#ifndef GPUOS_JIT_CASES8
+#define GPUOS_JIT_CASES8
+#endif
+#ifndef GPUOS_JIT_CASES1
+#define GPUOS_JIT_CASES1
+#endif
+
+#define GPUOS_CASE8(V) case V: op8<V>(A, B, R, p0, p1); return true;
+#define GPUOS_CASE1(V) case V: r = op1<V>(A, B, p0, p1); return true;
+#define GPUOS_ALL_EW(M) \
+  M(V_ADD) M(V_MUL) M(V_SUB) M(V_DIV0) M(V_DIV) M(V_MAX) M(V_MIN) M(V_POW) \
+  M(V_RELU) M(V_SIGMOID) M(V_TANH) M(V_EXP) M(V_LOG) M(V_SQRT) M(V_ABS) \
+  M(V_HARDSIGMOID) M(V_HARDSWISH) M(V_GELU) M(V_SIN) M(V_COS) M(V_LEAKY_RELU) \
+  M(V_CLAMP) M(V_ELU) M(V_SOFTPLUS) M(V_CLAMP_MIN) M(V_CLAMP_MAX) M(V_COPY)
+
+// Apply variant v to 8 lanes of values.  The switch is uniform per chunk.
+__device__ __forceinline__ bool ew_apply8(int v, const float* A, const float* B, float* R,
+                                          float p0, float p1) {
+  switch (v) {
+    GPUOS_ALL_EW(GPUOS_CASE8)
+    GPUOS_JIT_CASES8
+    default: return false;
+  }
+}
+
+__device__ __forceinline__ bool ew_apply1(int v, float A, float B, float& r, float p0, float p1) {
+  switch (v) {
+    GPUOS_ALL_EW(GPUOS_CASE1)
+    GPUOS_JIT_CASES1
+    default: return false;
+  }
+}
+
+// ---- scalar load / store (element offsets) -------------------------------
+__device__ __forceinline__ float ld1(uint64_t base, int dt, int64_t off) {
+  if (dt == kF32) return reinterpret_cast<const float*>(base)[off];
+  if (dt == kF16) return __half2float(reinterpret_cast<const __half*>(base)[off]);
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[off]);
+}
+
+__device__ __forceinline__ void st1(uint64_t base, int dt, int64_t off, float v) {
+  if (dt == kF32) reinterpret_cast<float*>(base)[off] = v;
+  else if (dt == kF16) reinterpret_cast<__half*>(base)[off] = __float2half_rn(v);
+  else reinterpret_cast<__nv_bfloat16*>(base)[off] = __float2bfloat16(v);
+}
+
+// ---- 8-element vector load / store: element offset `e` is a multiple of 8 and
+// the address is 16-byte aligned (checked on the host before RF_VEC is set).
+__device__ __forceinline__ void bf2_to_f(uint32_t u, float& lo, float& hi) {
+  lo = __uint_as_float(u << 16);
+  hi = __uint_as_float(u & 0xffff0000u);
+}
+
+__device__ __forceinline__ void ld8(uint64_t base, int dt, int64_t e, float* v) {
+  if (dt == kF32) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e);
+    float4 x = p[0], y = p[1];
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+  } else {
+    uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + e);
+    if (dt == kF16) {
+      float2 f;
+      f = __half22float2(*reinterpret_cast<const __half2*>(&u.x)); v[0] = f.x; v[1] = f.y;
+      f = __half22float2(*reinterpret_cast<const __half2*>(&u.y)); v[2] = f.x; v[3] = f.y;
+      f = __half22float2(*reinterpret_cast<const __half2*>(&u.z)); v[4] = f.x; v[5] = f.y;
+      f = __half22float2(*reinterpret_cast<const __half2*>(&u.w)); v[6] = f.x; v[7] = f.y;
+    } else {
+      bf2_to_f(u.x, v[0], v[1]); bf2_to_f(u.y, v[2], v[3]);
+      bf2_to_f(u.z, v[4], v[5]); bf2_to_f(u.w, v[6], v[7]);
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t f2_to_bf2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void st8(uint64_t base, int dt, int64_t e, const float* v) {
+  if (dt == kF32) {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + e);
+    p[0] = make_float4(v[0], v[1], v[2], v[3]);
+    p[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 u;
+    if (dt == kF16) {
+      u.x = f2_to_h2(v[0], v[1]); u.y = f2_to_h2(v[2], v[3]);
+      u.z = f2_to_h2(v[4], v[5]); u.w = f2_to_h2(v[6], v[7]);
+    } else {
+      u.x = f2_to_bf2(v[0], v[1]); u.y = f2_to_bf2(v[2], v[3]);
+      u.z = f2_to_bf2(v[4], v[5]); u.w = f2_to_bf2(v[6], v[7]);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(base) + e) = u;
+  }
+}
+
+}  // namespace gpuos

@@ -1,0 +1,1481 @@
+// Host runtime of the aggregated small-op executor and its C ABI.
+// See runtime.h for the structure and the reference correspondence.
+#include "runtime.h"
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstddef>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <thread>
+
+#if defined(__x86_64__)
+#include <immintrin.h>
+#define GPUOS_PAUSE() _mm_pause()
+#else
+#define GPUOS_PAUSE() std::this_thread::yield()
+#endif
+
+extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::Tables* tab,
+                                          volatile uint64_t* done_ring,
+                                          volatile uint64_t* retired_ring, uint64_t wait_limit_ns,
+                                          int grid, int block, cudaStream_t stream);
+extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, int block,
+                                           cudaStream_t stream);
+extern "C" cudaError_t gpuos_occupancy(int block, int* batch_blocks_per_sm,
+                                       int* worker_blocks_per_sm);
+
+namespace gpuos {
+
+namespace {
+
+thread_local std::string t_last_error;
+
+#define GCU(expr)                                                                     \
+  do {                                                                                \
+    cudaError_t e_ = (expr);                                                          \
+    if (e_ != cudaSuccess)                                                            \
+      throw GError(GPUOS_ECUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));  \
+  } while (0)
+
+constexpr uint64_t kDoneMask = (1ull << 56) - 1;
+
+inline bool dt_ok(int dt) { return dt == kF32 || dt == kF16 || dt == kBF16; }
+inline int esz(int dt) { return dt == kF32 ? 4 : 2; }
+inline uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+inline uint32_t pow2_ceil(uint64_t x) {
+  uint32_t p = 1;
+  while (p < x && p < (1u << 30)) p <<= 1;
+  return p;
+}
+
+void check_tensor(const gpuos_tensor& t, const char* what) {
+  if (t.ndim < 0 || t.ndim > kMaxDims)
+    throw GError(GPUOS_EINVAL, std::string(what) + ": ndim must be in [0, 8]");
+  if (!dt_ok(t.dtype))
+    throw GError(GPUOS_EINVAL, std::string(what) +
+                                   ": dtype must be float32, float16 or bfloat16 (code " +
+                                   std::to_string(t.dtype) + ")");
+  for (int d = 0; d < t.ndim; ++d)
+    if (t.sizes[d] < 0) throw GError(GPUOS_EINVAL, std::string(what) + ": negative size");
+}
+
+int64_t numel_of(const gpuos_tensor& t) {
+  int64_t n = 1;
+  for (int d = 0; d < t.ndim; ++d) n *= t.sizes[d];
+  return n;
+}
+
+Extent extent_of(const gpuos_tensor& t) {
+  int64_t lo = 0, hi = 0;
+  for (int d = 0; d < t.ndim; ++d) {
+    if (t.sizes[d] == 0) return Extent{};
+    const int64_t s = t.strides[d] * (t.sizes[d] - 1);
+    if (s < 0) lo += s; else hi += s;
+  }
+  const uint64_t base = reinterpret_cast<uint64_t>(t.data);
+  const int e = esz(t.dtype);
+  return Extent{base + (uint64_t)(lo * e), base + (uint64_t)((hi + 1) * e)};
+}
+
+// torch broadcasting of `t` onto the output shape: right-aligned, size-1
+// dims repeat with stride 0 (fill_tensorref, gpuos_ext.cpp:147-165, does the
+// alignment but keeps the input's own sizes; here the strides alone carry it).
+void broadcast_to(const gpuos_tensor& t, const gpuos_tensor& out, int64_t* st, const char* what) {
+  const int nd = out.ndim;
+  for (int d = 0; d < t.ndim - nd; ++d)
+    if (t.sizes[d] != 1)
+      throw GError(GPUOS_EINVAL, std::string(what) + ": has more dims than the output");
+  for (int d = 0; d < nd; ++d) {
+    const int od = nd - 1 - d, id = t.ndim - 1 - d;
+    const int64_t s_in = id >= 0 ? t.sizes[id] : 1;
+    const int64_t str = id >= 0 ? t.strides[id] : 0;
+    if (s_in == out.sizes[od]) st[od] = (s_in == 1) ? 0 : str;
+    else if (s_in == 1) st[od] = 0;
+    else
+      throw GError(GPUOS_EINVAL, std::string(what) + ": size " + std::to_string(s_in) +
+                                     " does not broadcast to " + std::to_string(out.sizes[od]));
+  }
+}
+
+double env_double(const char* name, double dflt) {
+  const char* v = std::getenv(name);
+  if (!v || !*v) return dflt;
+  return std::atof(v);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// helpers
+// ---------------------------------------------------------------------------
+uint32_t fdiv_magic(uint32_t d, uint32_t* shift) {
+  uint32_t s = 0;
+  while ((1ull << s) < d) ++s;
+  *shift = s;
+  return (uint32_t)((((1ull << 32) * ((1ull << s) - d)) / d) + 1);
+}
+
+bool IntervalSet::overlaps(const Extent& e) const {
+  if (e.empty() || m_.empty()) return false;
+  auto it = m_.upper_bound(e.lo);
+  if (it != m_.end() && it->first < e.hi) return true;
+  if (it != m_.begin()) {
+    --it;
+    if (it->second > e.lo) return true;
+  }
+  return false;
+}
+
+void IntervalSet::add(Extent e) {
+  if (e.empty()) return;
+  auto it = m_.upper_bound(e.lo);
+  if (it != m_.begin()) {
+    auto p = std::prev(it);
+    if (p->second >= e.lo) {
+      e.lo = p->first;
+      e.hi = std::max(e.hi, p->second);
+      it = m_.erase(p);
+    }
+  }
+  while (it != m_.end() && it->first <= e.hi) {
+    e.hi = std::max(e.hi, it->second);
+    it = m_.erase(it);
+  }
+  m_.emplace(e.lo, e.hi);
+}
+
+bool RingAlloc::alloc(uint64_t size, uint64_t tag, uint64_t* off) {
+  if (size == 0) { *off = 0; return true; }
+  if (size > cap_) return false;
+  if (live_.empty()) {
+    *off = 0;
+    live_.push_back({0, size, tag});
+    return true;
+  }
+  const uint64_t head = live_.front().off;
+  const uint64_t tail = live_.back().off + live_.back().size;
+  if (tail > head || (tail == head && false)) {
+    // [head, tail) in use, free: [tail, cap) and [0, head)
+    if (cap_ - tail >= size) { *off = tail; live_.push_back({tail, size, tag}); return true; }
+    if (head >= size) { *off = 0; live_.push_back({0, size, tag}); return true; }
+    return false;
+  }
+  // wrapped: in use [head, cap) and [0, tail), free [tail, head)
+  if (head - tail >= size) { *off = tail; live_.push_back({tail, size, tag}); return true; }
+  return false;
+}
+
+void RingAlloc::free_before(uint64_t upto) {
+  while (!live_.empty() && live_.front().tag < upto) live_.pop_front();
+}
+
+// Operator names accepted by gpuos_variant_by_name (and the Python layer).
+int variant_by_name(const std::string& n) {
+  static const std::unordered_map<std::string, int> m = {
+      {"add", V_ADD}, {"mul", V_MUL}, {"sub", V_SUB}, {"div0", V_DIV0}, {"batch_div", V_DIV0},
+      {"div", V_DIV}, {"maximum", V_MAX}, {"minimum", V_MIN}, {"pow", V_POW}, {"relu", V_RELU},
+      {"sigmoid", V_SIGMOID}, {"tanh", V_TANH}, {"exp", V_EXP}, {"log", V_LOG},
+      {"sqrt", V_SQRT}, {"abs", V_ABS}, {"hardsigmoid", V_HARDSIGMOID},
+      {"hardswish", V_HARDSWISH}, {"gelu", V_GELU}, {"sin", V_SIN}, {"cos", V_COS},
+      {"leaky_relu", V_LEAKY_RELU}, {"clamp", V_CLAMP}, {"hardtanh", V_CLAMP}, {"elu", V_ELU},
+      {"softplus", V_SOFTPLUS}, {"clamp_min", V_CLAMP_MIN}, {"clamp_max", V_CLAMP_MAX},
+      {"copy", V_COPY}, {"sum", V_SUM}, {"mean", V_MEAN}};
+  auto it = m.find(n);
+  return it == m.end() ? -1 : it->second;
+}
+
+// The expression strings the reference scheduler registers
+// (pytorch_ext/scheduler.py:145-153, 192-205, 244-290), whitespace removed,
+// '#' standing for a float literal with an 'f' suffix.
+namespace {
+struct ExprPat {
+  const char* pat;
+  int variant;
+  int arity;
+};
+const ExprPat kExprPats[] = {
+    {"(A+B)", V_ADD, 2},
+    {"(A-B)", V_SUB, 2},
+    {"(A*B)", V_MUL, 2},
+    {"(A/B)", V_DIV, 2},
+    {"(A>B?A:B)", V_MAX, 2},
+    {"(A<B?A:B)", V_MIN, 2},
+    {"powf(A,B)", V_POW, 2},
+    {"(A>0.f?A:0.f)", V_RELU, 1},
+    {"1.f/(1.f+expf(-A))", V_SIGMOID, 1},
+    {"tanhf(A)", V_TANH, 1},
+    {"expf(A)", V_EXP, 1},
+    {"logf(A)", V_LOG, 1},
+    {"sqrtf(A)", V_SQRT, 1},
+    {"fabsf(A)", V_ABS, 1},
+    {"fminf(fmaxf(0.2f*A+0.5f,0.f),1.f)", V_HARDSIGMOID, 1},
+    {"A*fminf(fmaxf(A/6.f+0.5f,0.f),1.f)", V_HARDSWISH, 1},
+    {"0.5f*A*(1.f+tanhf(0.79788456f*(A+0.044715f*A*A*A)))", V_GELU, 1},
+    {"sinf(A)", V_SIN, 1},
+    {"cosf(A)", V_COS, 1},
+    {"(A>=0.f?A:#*A)", V_LEAKY_RELU, 1},
+    {"fminf(fmaxf(A,#),#)", V_CLAMP, 1},
+    {"(A>0.f?A:#*(expf(A)-1.f))", V_ELU, 1},
+    {"(log1pf(expf(#*A))/#)", V_SOFTPLUS, 1},
+    {"fmaxf(A,#)", V_CLAMP_MIN, 1},
+    {"fminf(A,#)", V_CLAMP_MAX, 1},
+    {"A", V_COPY, 1},
+    {"(A)", V_COPY, 1},
+};
+
+// parse a C float literal with an 'f' suffix at s[i]; returns chars consumed
+size_t parse_flit(const std::string& s, size_t i, float* out) {
+  size_t j = i;
+  if (j < s.size() && (s[j] == '+' || s[j] == '-')) ++j;
+  size_t digits = 0;
+  while (j < s.size() && std::isdigit((unsigned char)s[j])) { ++j; ++digits; }
+  if (j < s.size() && s[j] == '.') {
+    ++j;
+    while (j < s.size() && std::isdigit((unsigned char)s[j])) { ++j; ++digits; }
+  }
+  if (digits == 0) return 0;
+  if (j < s.size() && (s[j] == 'e' || s[j] == 'E')) {
+    size_t k = j + 1;
+    if (k < s.size() && (s[k] == '+' || s[k] == '-')) ++k;
+    size_t ed = 0;
+    while (k < s.size() && std::isdigit((unsigned char)s[k])) { ++k; ++ed; }
+    if (ed == 0) return 0;
+    j = k;
+  }
+  if (j >= s.size() || s[j] != 'f') return 0;
+  *out = std::strtof(s.substr(i, j - i).c_str(), nullptr);
+  return j + 1 - i;
+}
+}  // namespace
+
+int match_builtin_expr(const std::string& expr, int arity, float* p0, float* p1) {
+  std::string e;
+  for (char c : expr)
+    if (!std::isspace((unsigned char)c)) e.push_back(c);
+  for (const ExprPat& p : kExprPats) {
+    if (p.arity != arity) continue;
+    const std::string pat = p.pat;
+    float vals[2] = {0.f, 0.f};
+    int nv = 0;
+    size_t i = 0, j = 0;
+    bool ok = true;
+    while (ok && j < pat.size()) {
+      if (pat[j] == '#') {
+        float v = 0.f;
+        const size_t n = parse_flit(e, i, &v);
+        if (n == 0 || nv >= 2) { ok = false; break; }
+        vals[nv++] = v;
+        i += n;
+        ++j;
+      } else if (i < e.size() && e[i] == pat[j]) {
+        ++i;
+        ++j;
+      } else {
+        ok = false;
+      }
+    }
+    if (!ok || i != e.size()) continue;
+    if (p.variant == V_SOFTPLUS && vals[0] != vals[1]) continue;
+    *p0 = vals[0];
+    *p1 = vals[1];
+    return p.variant;
+  }
+  return -1;
+}
+
+// ---------------------------------------------------------------------------
+// Executor
+// ---------------------------------------------------------------------------
+namespace {
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+}  // namespace
+
+Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_(opt) {
+  DeviceGuard g(device);
+  if (opt_.capacity <= 0) opt_.capacity = 4096;
+  if (opt_.threads_per_block <= 0) opt_.threads_per_block = 256;
+  if (opt_.max_batch <= 0) opt_.max_batch = (int)env_double("GPUOS_BATCH_SHARD", 512);
+  opt_.max_batch = std::min(opt_.max_batch, kMaxReqPerBatch);
+  if (opt_.mode != GPUOS_MODE_STREAM) opt_.mode = GPUOS_MODE_PERSISTENT;
+  int tpb = opt_.threads_per_block;
+  if (tpb % 32 != 0 || tpb < 64 || tpb > 1024)
+    throw GError(GPUOS_EINVAL, "threads_per_block must be a multiple of 32 in [64, 1024]");
+  double idle_ms = opt_.idle_ms > 0 ? opt_.idle_ms : env_double("GPUOS_IDLE_MS", 100.0);
+  idle_ms = std::min(std::max(idle_ms, 1.0), 60000.0);
+  idle_ns_ = (uint64_t)(idle_ms * 1e6);
+  sync_timeout_s_ = opt_.sync_timeout_s > 0 ? opt_.sync_timeout_s
+                                            : env_double("GPUOS_SYNC_TIMEOUT_S", 60.0);
+  // every wait inside a kernel gives up after this long and reports an error
+  wait_limit_ns_ = (uint64_t)(std::min(std::max(sync_timeout_s_, 1.0), 10.0) * 1e9);
+
+  GCU(cudaFree(nullptr));
+  GCU(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, device));
+  block_ = tpb;
+  int bbps = 0, wbps = 0;
+  GCU(gpuos_occupancy(block_, &bbps, &wbps));
+  if (bbps < 1 || wbps < 1) throw GError(GPUOS_ECUDA, "kernel cannot be resident with this block size");
+  batch_bps_ = bbps;
+  // The worker keeps about 16 warps per SM: enough bytes in flight to stream
+  // HBM, while leaving room for other kernels next to the resident grid.
+  int wanted = opt_.blocks_per_sm > 0 ? opt_.blocks_per_sm : std::max(1, 512 / block_);
+  wanted = std::min(wanted, wbps);
+  grid_ = sm_count_ * wanted;
+
+  GCU(cudaStreamCreateWithFlags(&s_worker_, cudaStreamNonBlocking));
+  GCU(cudaStreamCreateWithFlags(&s_ctrl_, cudaStreamNonBlocking));
+  GCU(cudaStreamCreateWithFlags(&s_own_, cudaStreamNonBlocking));
+  GCU(cudaEventCreateWithFlags(&last_event_, cudaEventDisableTiming));
+
+  // staging arena (pinned, mapped) and its device mirror
+  arena_bytes_ = align_up(std::max<uint64_t>(16ull << 20, (uint64_t)opt_.capacity * 1024), 1 << 20);
+  GCU(cudaHostAlloc(reinterpret_cast<void**>(&arena_), arena_bytes_, cudaHostAllocMapped));
+  GCU(cudaHostGetDevicePointer(reinterpret_cast<void**>(&arena_dev_), arena_, 0));
+  GCU(cudaMalloc(reinterpret_cast<void**>(&ring_), arena_bytes_));
+  arena_alloc_.init(arena_bytes_);
+
+  // host control block + rings
+  const size_t hb = align_up(sizeof(HostCtrl), 256) + align_up(sizeof(Pub) * kDoneRing, 256) +
+                    2 * sizeof(uint64_t) * kDoneRing + 256;
+  GCU(cudaHostAlloc(reinterpret_cast<void**>(&hostblk_), hb, cudaHostAllocMapped));
+  std::memset(hostblk_, 0, hb);
+  GCU(cudaHostGetDevicePointer(reinterpret_cast<void**>(&hostblk_dev_), hostblk_, 0));
+  size_t o = 0;
+  hctrl_ = reinterpret_cast<HostCtrl*>(hostblk_ + o);
+  o += align_up(sizeof(HostCtrl), 256);
+  pub_ = reinterpret_cast<Pub*>(hostblk_ + o);
+  o += align_up(sizeof(Pub) * kDoneRing, 256);
+  done_ring_ = reinterpret_cast<volatile uint64_t*>(hostblk_ + o);
+  o += sizeof(uint64_t) * kDoneRing;
+  retired_ring_ = reinterpret_cast<volatile uint64_t*>(hostblk_ + o);
+  o += sizeof(uint64_t) * kDoneRing;
+  *reinterpret_cast<uint64_t*>(hostblk_ + o) = UINT64_MAX;  // source of the stop_at reset
+
+  GCU(cudaMalloc(reinterpret_cast<void**>(&dctrl_), sizeof(DevCtrl)));
+  GCU(cudaMemset(dctrl_, 0, sizeof(DevCtrl)));
+
+  // jump table: identity alias, slot 0 = add, slot 1 = mul as the reference's
+  // init_builtin_ops (persistent_kernel.cu:115-130); slot 10 is the batch
+  // operator there and stays reserved here.
+  for (int i = 0; i < kMaxSlots; ++i) {
+    tab_.alias[i] = i;
+    tab_.slot[i] = SlotEntry{V_NONE, 0.f, 0.f, 0};
+  }
+  tab_.slot[0] = SlotEntry{V_ADD, 0.f, 0.f, 2};
+  tab_.slot[1] = SlotEntry{V_MUL, 0.f, 0.f, 2};
+  GCU(cudaMalloc(reinterpret_cast<void**>(&tab_dev_), sizeof(Tables)));
+  upload_tables_locked();
+  GCU(cudaDeviceSynchronize());
+  started_ = true;
+  if (opt_.mode == GPUOS_MODE_PERSISTENT) launch_worker_locked(0);
+}
+
+Executor::~Executor() {
+  try {
+    shutdown();
+  } catch (...) {
+  }
+}
+
+void Executor::upload_tables_locked() {
+  DeviceGuard g(device_);
+  GCU(cudaMemcpyAsync(tab_dev_, &tab_, sizeof(Tables), cudaMemcpyHostToDevice, s_ctrl_));
+  GCU(cudaStreamSynchronize(s_ctrl_));
+}
+
+void Executor::ensure_scratch_locked() {
+  if (partials_) return;
+  DeviceGuard g(device_);
+  partials_cap_ = 16ull << 20;  // floats
+  counters_cap_ = 4ull << 20;   // u32
+  GCU(cudaMalloc(reinterpret_cast<void**>(&partials_), partials_cap_ * sizeof(float)));
+  GCU(cudaMalloc(reinterpret_cast<void**>(&counters_), counters_cap_ * sizeof(uint32_t)));
+  GCU(cudaMemset(counters_, 0, counters_cap_ * sizeof(uint32_t)));
+  GCU(cudaDeviceSynchronize());
+  part_alloc_.init(partials_cap_);
+  cnt_alloc_.init(counters_cap_);
+}
+
+// ---- request building -----------------------------------------------------
+void build_ew(Pending& p, int op, bool is_slot, float p0, float p1,
+                        const gpuos_tensor* a, const gpuos_tensor* b, const gpuos_tensor& out) {
+  if (!a) throw GError(GPUOS_EINVAL, "input A is required");
+  check_tensor(*a, "input A");
+  if (b) check_tensor(*b, "input B");
+  check_tensor(out, "output");
+  const int nd = out.ndim;
+  int64_t sa[kMaxDims] = {0}, sb[kMaxDims] = {0};
+  broadcast_to(*a, out, sa, "input A");
+  if (b) broadcast_to(*b, out, sb, "input B");
+  const int64_t numel = numel_of(out);
+
+  struct Dim { int64_t n, a, b, o; };
+  Dim dims[kMaxDims];
+  int k = 0;
+  for (int d = 0; d < nd; ++d)
+    if (out.sizes[d] != 1) dims[k++] = Dim{out.sizes[d], sa[d], sb[d], out.strides[d]};
+  Dim cd[kMaxDims];
+  int m = 0;
+  for (int i = 0; i < k; ++i) {
+    const Dim& x = dims[i];
+    if (m > 0 && cd[m - 1].a == x.a * x.n && cd[m - 1].b == x.b * x.n && cd[m - 1].o == x.o * x.n) {
+      cd[m - 1] = Dim{cd[m - 1].n * x.n, x.a, x.b, x.o};
+    } else {
+      cd[m++] = x;
+    }
+  }
+
+  Req& q = p.r;
+  std::memset(&q, 0, sizeof(q));
+  q.op = (uint16_t)op;
+  q.kind = RK_EW;
+  q.dta = (uint8_t)a->dtype;
+  q.dtb = (uint8_t)(b ? b->dtype : a->dtype);
+  q.dto = (uint8_t)out.dtype;
+  q.flags = (uint8_t)((b ? RF_HAS_B : 0) | (is_slot ? RF_SLOT : 0));
+  q.p0 = p0;
+  q.p1 = p1;
+  q.numel = numel;
+  q.a = reinterpret_cast<uint64_t>(a->data);
+  q.b = b ? reinterpret_cast<uint64_t>(b->data) : 0;
+  q.o = reinterpret_cast<uint64_t>(out.data);
+  const int ea = esz(a->dtype), eb = b ? esz(b->dtype) : 0, eo = esz(out.dtype);
+
+  bool a_sc = m > 0, b_sc = b != nullptr && m > 0;
+  for (int i = 0; i < m; ++i) {
+    if (cd[i].a != 0) a_sc = false;
+    if (cd[i].b != 0) b_sc = false;
+  }
+  auto al16 = [](uint64_t x) { return (x & 15) == 0; };
+
+  if (m <= 1 && (m == 0 || cd[0].o == 1) &&
+      (m == 0 || cd[0].a == 0 || cd[0].a == 1) &&
+      (!b || m == 0 || cd[0].b == 0 || cd[0].b == 1)) {
+    q.layout = EL_CONTIG;
+    if (a_sc) q.flags |= RF_A_SCALAR;
+    if (b_sc) q.flags |= RF_B_SCALAR;
+    bool vec = al16(q.o) && (a_sc || al16(q.a)) && (!b || b_sc || al16(q.b));
+    if (vec) q.flags |= RF_VEC;
+  } else if (m <= 2 && cd[m - 1].o == 1) {
+    const int64_t R = (m == 2) ? cd[0].n : 1, N = cd[m - 1].n;
+    q.layout = EL_ROW2D;
+    q.inner = N;
+    q.sa_row = m == 2 ? cd[0].a : 0;
+    q.sb_row = m == 2 ? cd[0].b : 0;
+    q.so_row = m == 2 ? cd[0].o : 0;
+    q.sa_in = cd[m - 1].a;
+    q.sb_in = cd[m - 1].b;
+    if (a_sc) q.flags |= RF_A_SCALAR;
+    if (b_sc) q.flags |= RF_B_SCALAR;
+    auto opnd_vec = [&](bool sc, uint64_t ptr, int64_t srow, int64_t sin, int e) {
+      if (sc || sin == 0) return true;
+      if (sin != 1) return false;
+      return al16(ptr) && (R == 1 || ((srow * e) & 15) == 0);
+    };
+    bool vec = (N % 8 == 0) && opnd_vec(false, q.o, q.so_row, 1, eo) &&
+               opnd_vec(a_sc, q.a, q.sa_row, q.sa_in, ea) &&
+               (!b || opnd_vec(b_sc, q.b, q.sb_row, q.sb_in, eb));
+    if (vec) q.flags |= RF_VEC;
+    if (numel >= (1ll << 31) || N >= (1ll << 31)) {
+      q.flags |= RF_BIG;
+    } else {
+      uint32_t s = 0;
+      q.fdiv_m = fdiv_magic((uint32_t)N, &s);
+      q.fdiv_s = s;
+    }
+  } else {
+    q.layout = EL_STRIDED;
+    p.has_ext = true;
+    std::memset(&p.ext, 0, sizeof(p.ext));
+    p.ext.ndim = m;
+    for (int i = 0; i < m; ++i) {
+      p.ext.sizes[i] = cd[i].n;
+      p.ext.sa[i] = cd[i].a;
+      p.ext.sb[i] = cd[i].b;
+      p.ext.so[i] = cd[i].o;
+    }
+  }
+  const int bpe = ea + eb + eo;
+  uint32_t ce = q.layout == EL_STRIDED ? 1024u : (bpe >= 10 ? 2048u : 4096u);
+  q.chunk = ce;
+  p.nchunk = (uint32_t)((numel + ce - 1) / ce);
+  p.out_ext = extent_of(out);
+  p.in_ext[0] = extent_of(*a);
+  p.nin = 1;
+  if (b) {
+    p.in_ext[1] = extent_of(*b);
+    p.nin = 2;
+  }
+}
+
+void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
+                            const gpuos_tensor& out, const int32_t* axes, int naxes,
+                            bool keepdim) {
+  check_tensor(x, "input");
+  check_tensor(out, "output");
+  const int nd = x.ndim;
+  bool red[kMaxDims] = {false};
+  int nred = 0;
+  for (int i = 0; i < naxes; ++i) {
+    int ax = axes[i];
+    if (ax < 0) ax += nd;
+    if (ax < 0 || ax >= nd) throw GError(GPUOS_EINVAL, "reduction axis out of range");
+    if (!red[ax]) { red[ax] = true; ++nred; }
+  }
+  const int out_nd = keepdim ? nd : nd - nred;
+  if (out.ndim != out_nd)
+    throw GError(GPUOS_EINVAL, "output has " + std::to_string(out.ndim) + " dims, expected " +
+                                   std::to_string(out_nd));
+  struct KD { int64_t n, sa, so; };
+  struct RD { int64_t n, s; };
+  KD kd[kMaxDims];
+  RD rd[kMaxDims];
+  int nk = 0, nr = 0, od = 0;
+  int64_t C = 1;
+  for (int d = 0; d < nd; ++d) {
+    if (red[d]) {
+      if (keepdim) {
+        if (out.sizes[od] != 1) throw GError(GPUOS_EINVAL, "keepdim output must have size 1 on reduced axes");
+        ++od;
+      }
+      C *= x.sizes[d];
+      if (x.sizes[d] != 1) rd[nr++] = RD{x.sizes[d], x.strides[d]};
+    } else {
+      if (out.sizes[od] != x.sizes[d]) throw GError(GPUOS_EINVAL, "output shape does not match input");
+      if (x.sizes[d] != 1) kd[nk++] = KD{x.sizes[d], x.strides[d], out.strides[od]};
+      ++od;
+    }
+  }
+  // coalesce kept dims (input and output strides together) and reduced dims
+  KD ck[kMaxDims];
+  RD cr[kMaxDims];
+  int mk = 0, mr = 0;
+  for (int i = 0; i < nk; ++i) {
+    if (mk > 0 && ck[mk - 1].sa == kd[i].sa * kd[i].n && ck[mk - 1].so == kd[i].so * kd[i].n)
+      ck[mk - 1] = KD{ck[mk - 1].n * kd[i].n, kd[i].sa, kd[i].so};
+    else
+      ck[mk++] = kd[i];
+  }
+  for (int i = 0; i < nr; ++i) {
+    if (mr > 0 && cr[mr - 1].s == rd[i].s * rd[i].n)
+      cr[mr - 1] = RD{cr[mr - 1].n * rd[i].n, rd[i].s};
+    else
+      cr[mr++] = rd[i];
+  }
+  const int64_t R = numel_of(out);
+
+  Req& q = p.r;
+  std::memset(&q, 0, sizeof(q));
+  q.op = (uint16_t)op;
+  q.kind = RK_RED;
+  q.dta = (uint8_t)x.dtype;
+  q.dtb = (uint8_t)x.dtype;
+  q.dto = (uint8_t)out.dtype;
+  q.flags = (uint8_t)(is_slot ? RF_SLOT : 0);
+  q.numel = R;
+  q.inner = C;
+  q.a = reinterpret_cast<uint64_t>(x.data);
+  q.o = reinterpret_cast<uint64_t>(out.data);
+  q.nseg = 1;
+  const int e = esz(x.dtype);
+  constexpr int64_t kSeg = 8192;
+
+  if (mk <= 1 && mr <= 1) {
+    const int64_t sr = mk ? ck[0].sa : 0, so = mk ? ck[0].so : 0;
+    const int64_t sc = mr ? cr[0].s : 1;
+    q.sa_row = sr;
+    q.so_row = so;
+    q.sa_in = sc;
+    if (sc == 1) {
+      q.layout = RL_ROWS;
+      if ((q.a & 15) == 0 && (R == 1 || ((sr * e) & 15) == 0)) q.flags |= RF_VEC;
+      if (C <= kSeg) {
+        const uint32_t G = std::min<uint32_t>(32, pow2_ceil((uint64_t)std::max<int64_t>(1, (C + 15) / 16)));
+        const uint32_t per = 32 / G;
+        uint64_t rpc = (uint64_t)std::max<int64_t>(1, kSeg / std::max<int64_t>(C, 1));
+        rpc = std::max<uint64_t>(per, rpc / per * per);
+        q.rg = G;
+        q.chunk = (uint32_t)rpc;
+        p.nchunk = (uint32_t)((R + (int64_t)rpc - 1) / (int64_t)rpc);
+      } else {
+        q.rg = 32;
+        q.chunk = (uint32_t)kSeg;
+        q.nseg = (uint32_t)((C + kSeg - 1) / kSeg);
+        p.nchunk = (uint32_t)(R * q.nseg);
+        p.partials = (uint64_t)R * q.nseg;
+        p.counters = (uint64_t)R;
+      }
+    } else {
+      q.layout = RL_COLS;
+      const uint32_t rg = std::min<uint32_t>(32, pow2_ceil((uint64_t)std::max<int64_t>(R, 1)));
+      const uint32_t cl = 32 / rg;
+      int64_t seglen = std::max<int64_t>(cl, kSeg / rg);
+      int64_t nseg = std::max<int64_t>(1, (C + seglen - 1) / seglen);
+      if (nseg > 256) {
+        seglen = align_up((uint64_t)((C + 255) / 256), cl);
+        nseg = (C + seglen - 1) / seglen;
+      }
+      const int64_t ngroups = (R + rg - 1) / rg;
+      q.rg = rg;
+      q.chunk = (uint32_t)seglen;
+      q.nseg = (uint32_t)nseg;
+      p.nchunk = (uint32_t)(ngroups * nseg);
+      if (nseg > 1) {
+        p.partials = (uint64_t)(ngroups * nseg * rg);
+        p.counters = (uint64_t)ngroups;
+      }
+    }
+  } else {
+    q.layout = RL_GENERIC;
+    q.chunk = 32;
+    p.nchunk = (uint32_t)((R + 31) / 32);
+    p.has_ext = true;
+    std::memset(&p.ext, 0, sizeof(p.ext));
+    p.ext.ndim = mk;
+    p.ext.rdim = mr;
+    for (int i = 0; i < mk; ++i) {
+      p.ext.sizes[i] = ck[i].n;
+      p.ext.sa[i] = ck[i].sa;
+      p.ext.so[i] = ck[i].so;
+    }
+    for (int i = 0; i < mr; ++i) {
+      p.ext.rsizes[i] = cr[i].n;
+      p.ext.rstrides[i] = cr[i].s;
+    }
+  }
+  if ((uint64_t)p.nchunk * 1 > 0xffffffffull) throw GError(GPUOS_EINVAL, "request too large");
+  p.out_ext = extent_of(out);
+  p.in_ext[0] = extent_of(x);
+  p.nin = 1;
+}
+
+void Executor::submit_ew(int op, bool is_slot, float p0, float p1, const gpuos_tensor* a,
+                         const gpuos_tensor* b, const gpuos_tensor& out) {
+  Pending p;
+  build_ew(p, op, is_slot, p0, p1, a, b, out);
+  std::lock_guard<std::mutex> lk(mu_);
+  if (!started_) throw GError(GPUOS_ESTATE, "executor is shut down");
+  ++requests_;
+  if (p.nchunk == 0) return;  // empty output: nothing to do
+  pending_.push_back(p);
+}
+
+void Executor::submit_reduce(int op, bool is_slot, const gpuos_tensor& x,
+                             const gpuos_tensor& out, const int32_t* axes, int naxes,
+                             bool keepdim) {
+  Pending p;
+  build_reduce(p, op, is_slot, x, out, axes, naxes, keepdim);
+  std::lock_guard<std::mutex> lk(mu_);
+  if (!started_) throw GError(GPUOS_ESTATE, "executor is shut down");
+  ++requests_;
+  if (p.nchunk == 0) return;
+  pending_.push_back(p);
+}
+
+// The reference's Task (src/common.h:34-46), accepted as-is.
+namespace {
+struct RefTensorRef {
+  void* data;
+  int32_t dtype;
+  int32_t ndim;
+  int64_t sizes[8];
+  int64_t strides[8];
+};
+struct RefTask {
+  int32_t op, flags, ndim;
+  int64_t numel;
+  int32_t rrank;
+  int32_t r_axes[8];
+  int32_t r_keepdim;
+  RefTensorRef in0, in1, out0;
+};
+static_assert(sizeof(RefTensorRef) == 144, "TensorRef layout");
+static_assert(sizeof(RefTask) == 496, "Task layout");
+static_assert(offsetof(RefTask, numel) == 16 && offsetof(RefTask, rrank) == 24 &&
+                  offsetof(RefTask, in0) == 64 && offsetof(RefTask, in1) == 208 &&
+                  offsetof(RefTask, out0) == 352,
+              "Task field offsets");
+static_assert(sizeof(RefTensorRef) == sizeof(gpuos_tensor), "gpuos_tensor mirrors TensorRef");
+}  // namespace
+
+void Executor::submit_task(const void* task) {
+  RefTask t;
+  std::memcpy(&t, task, sizeof(t));
+  if (t.op == 10)
+    throw GError(GPUOS_EINVAL, "slot 10 is the batch operator; batches are built by gpuos_flush");
+  gpuos_tensor in0, in1, out0;
+  std::memcpy(&in0, &t.in0, sizeof(in0));
+  std::memcpy(&in1, &t.in1, sizeof(in1));
+  std::memcpy(&out0, &t.out0, sizeof(out0));
+  if (t.rrank > 0) {
+    if (t.rrank > 8) throw GError(GPUOS_EINVAL, "rrank > 8");
+    submit_reduce(t.op, true, in0, out0, t.r_axes, t.rrank, t.r_keepdim != 0);
+  } else {
+    submit_ew(t.op, true, 0.f, 0.f, &in0, t.in1.data ? &in1 : nullptr, out0);
+  }
+}
+
+// ---- batches ----------------------------------------------------------------
+void Executor::reclaim() {
+  while (done_wm_ < next_seq_) {
+    const uint64_t w = done_ring_[done_wm_ % kDoneRing];
+    if ((w & kDoneMask) != done_wm_ + 1) break;
+    const uint32_t e = (uint32_t)(w >> 56);
+    if (e) {
+      ++errors_;
+      if (err_seq_ == UINT64_MAX) err_seq_ = done_wm_;
+      err_bits_ |= e;
+    }
+    ++done_wm_;
+  }
+  while (retired_wm_ < next_seq_) {
+    if (retired_ring_[retired_wm_ % kDoneRing] != retired_wm_ + 1) break;
+    ++retired_wm_;
+  }
+  arena_alloc_.free_before(retired_wm_);
+  part_alloc_.free_before(retired_wm_);
+  cnt_alloc_.free_before(retired_wm_);
+  if (done_wm_ == next_seq_) {
+    live_out_.clear();
+    live_in_.clear();
+  }
+}
+
+bool Executor::wait_for_room_locked(std::unique_lock<std::mutex>& lk, uint64_t bytes,
+                                    uint64_t floats, uint64_t counters, uint64_t* arena_off,
+                                    uint64_t* part_off, uint64_t* cnt_off, uint64_t seq) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int it = 0;; ++it) {
+    reclaim();
+    if (next_seq_ - retired_wm_ < (uint64_t)kDoneRing - 1) {
+      uint64_t ao = 0, po = 0, co = 0;
+      if (arena_alloc_.alloc(bytes, seq, &ao)) {
+        const bool pok = floats == 0 || part_alloc_.alloc(floats, seq, &po);
+        const bool cok = pok && (counters == 0 || cnt_alloc_.alloc(counters, seq, &co));
+        if (pok && cok) {
+          *arena_off = ao;
+          *part_off = po;
+          *cnt_off = co;
+          return true;
+        }
+        // give back what this attempt took and wait for older batches to retire
+        if (pok && floats) part_alloc_.undo_last();
+        arena_alloc_.undo_last();
+      }
+    }
+    if (opt_.mode == GPUOS_MODE_PERSISTENT) ensure_worker_locked();
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > sync_timeout_s_) return false;
+    lk.unlock();
+    if (it < 64) GPUOS_PAUSE();
+    else if (it < 512) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(20));
+    lk.lock();
+  }
+}
+
+void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& reqs, size_t i,
+                       size_t j, cudaStream_t stream) {
+  const uint32_t n = (uint32_t)(j - i);
+  // hazards between the requests of this batch: a request that reads what an
+  // earlier request of its stage writes (or writes what it reads or writes)
+  // opens a new stage; chunks of a stage start after the previous stage is done.
+  std::vector<uint32_t> stage_first(n);
+  IntervalSet so, si;
+  uint32_t cur = 0;
+  bool staged = false, after_prev = false;
+  const bool check_live = opt_.mode == GPUOS_MODE_PERSISTENT && done_wm_ < next_seq_;
+  for (uint32_t r = 0; r < n; ++r) {
+    const Pending& p = reqs[i + r];
+    bool hz = so.overlaps(p.out_ext) || si.overlaps(p.out_ext);
+    for (int k = 0; k < p.nin && !hz; ++k) hz = so.overlaps(p.in_ext[k]);
+    if (hz) {
+      so.clear();
+      si.clear();
+      cur = r;
+      staged = true;
+    }
+    stage_first[r] = cur;
+    so.add(p.out_ext);
+    for (int k = 0; k < p.nin; ++k) si.add(p.in_ext[k]);
+    if (check_live && !after_prev) {
+      bool lz = live_out_.overlaps(p.out_ext) || live_in_.overlaps(p.out_ext);
+      for (int k = 0; k < p.nin && !lz; ++k) lz = live_out_.overlaps(p.in_ext[k]);
+      after_prev = lz;
+    }
+  }
+  // payload layout
+  std::vector<uint32_t> cb(n + 1);
+  uint64_t nchunk = 0, floats = 0, counters = 0;
+  uint32_t next = 0;
+  for (uint32_t r = 0; r < n; ++r) {
+    cb[r] = (uint32_t)nchunk;
+    nchunk += reqs[i + r].nchunk;
+    floats += reqs[i + r].partials;
+    counters += reqs[i + r].counters;
+    if (reqs[i + r].has_ext) ++next;
+  }
+  cb[n] = (uint32_t)nchunk;
+  if (nchunk > 0xffffffffull) throw GError(GPUOS_EINVAL, "batch too large");
+  const uint64_t rec_off = 128;
+  const uint64_t cb_off = rec_off + 128ull * n;
+  const uint64_t wait_off = cb_off + 4ull * (n + 1);
+  const uint64_t ext_off = align_up(wait_off + (staged ? 4ull * n : 0), 16);
+  const uint64_t bytes = align_up(ext_off + sizeof(ExtRec) * (uint64_t)next, 16);
+  if (floats || counters) ensure_scratch_locked();
+  if (bytes > arena_bytes_ || floats > partials_cap_ || counters > counters_cap_)
+    throw GError(GPUOS_EINVAL, "batch does not fit the staging memory");
+
+  const uint64_t seq = next_seq_;
+  uint64_t aoff = 0, poff = 0, coff = 0;
+  if (!wait_for_room_locked(lk, bytes, floats, counters, &aoff, &poff, &coff, seq))
+    throw GError(GPUOS_ETIMEOUT, "timed out waiting for staging memory");
+  uint8_t* base = arena_ + aoff;
+  std::memset(base, 0, 128);
+  BatchHdr* h = reinterpret_cast<BatchHdr*>(base);
+  h->seq = seq;
+  h->nreq = n;
+  h->nchunk = (uint32_t)nchunk;
+  h->rec_off = (uint32_t)rec_off;
+  h->cb_off = (uint32_t)cb_off;
+  h->bytes = (uint32_t)bytes;
+  h->flags = (staged ? BF_STAGED : 0u) | (after_prev ? BF_AFTER_PREV : 0u);
+  h->scratch = floats ? reinterpret_cast<uint64_t>(partials_ + poff) : 0;
+  h->counters = reinterpret_cast<uint64_t>(counters_);
+  h->wait_from = done_wm_;
+  h->dev_off = (uint32_t)aoff;
+  Req* recs = reinterpret_cast<Req*>(base + rec_off);
+  uint32_t* cbp = reinterpret_cast<uint32_t*>(base + cb_off);
+  ExtRec* ext = reinterpret_cast<ExtRec*>(base + ext_off);
+  uint64_t pf = 0, pc = coff, xi = 0;
+  for (uint32_t r = 0; r < n; ++r) {
+    Pending& p = reqs[i + r];
+    Req q = p.r;
+    if (p.has_ext) {
+      ext[xi] = p.ext;
+      q.ext = (uint32_t)(ext_off + sizeof(ExtRec) * xi);
+      ++xi;
+    }
+    if (p.partials) {
+      q.part = (uint32_t)pf;
+      pf += p.partials;
+    }
+    if (p.counters) {
+      q.cnt = (uint32_t)pc;
+      pc += p.counters;
+    }
+    recs[r] = q;
+  }
+  std::memcpy(cbp, cb.data(), 4ull * (n + 1));
+  if (staged) {
+    uint32_t* w = reinterpret_cast<uint32_t*>(base + wait_off);
+    for (uint32_t r = 0; r < n; ++r) w[r] = stage_first[r] ? cb[stage_first[r]] : 0u;
+  }
+  next_seq_ = seq + 1;
+
+  if (opt_.mode == GPUOS_MODE_PERSISTENT) {
+    Pub& pb = pub_[seq % kDoneRing];
+    pb.seq = seq;
+    pb.off = (uint32_t)aoff;
+    pb.bytes = (uint32_t)bytes;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    hctrl_->tail = seq + 1;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    for (uint32_t r = 0; r < n; ++r) {
+      live_out_.add(reqs[i + r].out_ext);
+      for (int k = 0; k < reqs[i + r].nin; ++k) live_in_.add(reqs[i + r].in_ext[k]);
+    }
+    ensure_worker_locked();
+  } else {
+    DeviceGuard g(device_);
+    if (last_stream_ && stream != last_stream_ && done_wm_ < seq) {
+      GCU(cudaEventRecord(last_event_, last_stream_));
+      GCU(cudaStreamWaitEvent(stream, last_event_, 0));
+    }
+    GCU(cudaMemcpyAsync(ring_ + aoff, arena_ + aoff, bytes, cudaMemcpyHostToDevice, stream));
+    const int wpb = block_ / 32;
+    int grid = (int)std::min<uint64_t>((uint64_t)sm_count_ * batch_bps_, (nchunk + wpb - 1) / wpb);
+    grid = std::max(grid, 1);
+    volatile uint64_t* dr = reinterpret_cast<volatile uint64_t*>(
+        hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));
+    volatile uint64_t* rr = reinterpret_cast<volatile uint64_t*>(
+        hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(retired_ring_) - hostblk_));
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (timing_) {
+      for (cudaEvent_t* e : {&e0, &e1}) {
+        if (ev_pool_.empty()) {
+          GCU(cudaEventCreate(e));
+        } else {
+          *e = ev_pool_.back();
+          ev_pool_.pop_back();
+        }
+      }
+      GCU(cudaEventRecord(e0, stream));
+    }
+    GCU(gpuos_launch_batch(ring_ + aoff, tab_dev_, dr, rr, wait_limit_ns_, grid, block_, stream));
+    if (timing_) {
+      GCU(cudaEventRecord(e1, stream));
+      timed_.emplace_back(e0, e1);
+    }
+    last_stream_ = stream;
+  }
+}
+
+uint64_t Executor::flush(bool sync, cudaStream_t stream) {
+  uint64_t ticket;
+  {
+    std::unique_lock<std::mutex> lk(mu_);
+    if (!started_) throw GError(GPUOS_ESTATE, "executor is shut down");
+    std::vector<Pending> reqs;
+    reqs.swap(pending_);
+    if (!reqs.empty()) {
+      DeviceGuard g(device_);
+      if (!stream) stream = s_own_;
+      if (opt_.mode == GPUOS_MODE_PERSISTENT && stream != s_own_) {
+        // the worker reads the inputs as soon as the doorbell rings, so work
+        // still queued on the producer stream must finish first
+        cudaError_t qs = cudaStreamQuery(stream);
+        if (qs == cudaErrorNotReady) GCU(cudaStreamSynchronize(stream));
+        else if (qs != cudaSuccess) GCU(qs);
+      }
+      size_t i = 0;
+      const uint64_t budget = arena_bytes_ / 4;
+      while (i < reqs.size()) {
+        size_t j = i;
+        uint64_t bytes = 256, floats = 0, cnts = 0, chunks = 0;
+        while (j < reqs.size() && j - i < (size_t)opt_.max_batch) {
+          const Pending& p = reqs[j];
+          const uint64_t b = 136 + (p.has_ext ? sizeof(ExtRec) : 0);
+          if (j > i && (bytes + b > budget || floats + p.partials > (16ull << 20) / 2 ||
+                        cnts + p.counters > (4ull << 20) / 2 ||
+                        chunks + p.nchunk > 0x7fffffffull))
+            break;
+          bytes += b;
+          floats += p.partials;
+          cnts += p.counters;
+          chunks += p.nchunk;
+          ++j;
+        }
+        publish(lk, reqs, i, j, stream);
+        i = j;
+      }
+    }
+    ticket = next_seq_;
+  }
+  if (sync) wait(ticket, sync_timeout_s_);
+  return ticket;
+}
+
+void Executor::wait(uint64_t ticket, double timeout_s) {
+  if (timeout_s <= 0) timeout_s = sync_timeout_s_;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int it = 0;; ++it) {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      reclaim();
+      if (done_wm_ >= ticket) {
+        if (err_seq_ != UINT64_MAX && err_seq_ < ticket) {
+          const uint32_t e = err_bits_;
+          err_seq_ = UINT64_MAX;
+          err_bits_ = 0;
+          std::string why;
+          if (e & ERR_BAD_OP) why += " a request used a slot with no registered operator;";
+          if (e & ERR_BAD_KIND) why += " a slot's operator does not fit the request kind;";
+          if (e & ERR_STAGE_TIMEOUT) why += " a stage barrier wait timed out;";
+          throw GError(GPUOS_EDEVICE, "gpuos batch error:" + why);
+        }
+        return;
+      }
+      if (opt_.mode == GPUOS_MODE_PERSISTENT) ensure_worker_locked();
+    }
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_s)
+      throw GError(GPUOS_ETIMEOUT, "timed out waiting for batch completion (done " +
+                                       std::to_string(done_wm_) + " of " +
+                                       std::to_string(ticket) + ")");
+    if (it < 256) GPUOS_PAUSE();
+    else if (it < 4096) std::this_thread::yield();
+    else std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+// ---- persistent worker -----------------------------------------------------
+void Executor::launch_worker_locked(uint64_t start) {
+  DeviceGuard g(device_);
+  hctrl_->running = 1u;
+  hctrl_->exit_reason = 0u;
+  hctrl_->idle_ns = idle_ns_;
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  const uint8_t* stop_src = hostblk_ + align_up(sizeof(HostCtrl), 256) +
+                            align_up(sizeof(Pub) * kDoneRing, 256) +
+                            2 * sizeof(uint64_t) * kDoneRing;
+  GCU(cudaMemcpyAsync(&dctrl_->stop_at, stop_src, sizeof(uint64_t), cudaMemcpyHostToDevice,
+                      s_worker_));
+  WorkerArgs w;
+  w.ring = ring_;
+  w.arena = arena_dev_;
+  w.hctrl = reinterpret_cast<volatile HostCtrl*>(hostblk_dev_);
+  w.pub = reinterpret_cast<const volatile Pub*>(
+      hostblk_dev_ + (reinterpret_cast<uint8_t*>(pub_) - hostblk_));
+  w.dctrl = dctrl_;
+  w.tab = tab_dev_;
+  w.done_ring = reinterpret_cast<volatile uint64_t*>(
+      hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));
+  w.retired_ring = reinterpret_cast<volatile uint64_t*>(
+      hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(retired_ring_) - hostblk_));
+  w.start_seq = start;
+  w.wait_limit_ns = wait_limit_ns_;
+  w.idle_ns = idle_ns_;
+  GCU(gpuos_launch_worker(&w, grid_, block_, s_worker_));
+  worker_launched_ = true;
+  ++relaunches_;
+}
+
+void Executor::ensure_worker_locked() {
+  if (opt_.mode != GPUOS_MODE_PERSISTENT || !started_) return;
+  DeviceGuard g(device_);
+  if (worker_launched_) {
+    cudaError_t q = cudaStreamQuery(s_worker_);
+    if (q == cudaErrorNotReady) {
+      if (hctrl_->running) return;
+      if (hctrl_->staged >= next_seq_) return;
+      // stopping while work is pending: let it finish exiting (bounded)
+      const auto t0 = std::chrono::steady_clock::now();
+      while ((q = cudaStreamQuery(s_worker_)) == cudaErrorNotReady) {
+        const double el =
+            std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (el > sync_timeout_s_) throw GError(GPUOS_ETIMEOUT, "persistent worker did not exit");
+        std::this_thread::yield();
+      }
+    }
+    if (q != cudaSuccess) GCU(q);
+    worker_launched_ = false;
+  }
+  if (hctrl_->staged < next_seq_) launch_worker_locked(hctrl_->staged);
+}
+
+bool Executor::worker_alive() {
+  std::lock_guard<std::mutex> lk(mu_);
+  if (opt_.mode != GPUOS_MODE_PERSISTENT || !started_ || !worker_launched_) return false;
+  DeviceGuard g(device_);
+  cudaError_t q = cudaStreamQuery(s_worker_);
+  if (q == cudaErrorNotReady) return true;
+  if (q != cudaSuccess) GCU(q);
+  worker_launched_ = false;
+  return false;
+}
+
+// ---- jump table --------------------------------------------------------------
+int Executor::register_elementwise(const std::string& key, const std::string& expr, int arity) {
+  std::lock_guard<std::mutex> lk(mu_);
+  auto it = slot_of_key_.find(key);
+  if (it != slot_of_key_.end()) return it->second;
+  if (arity != 1 && arity != 2) throw GError(GPUOS_EINVAL, "arity must be 1 or 2");
+  float p0 = 0.f, p1 = 0.f;
+  const int v = match_builtin_expr(expr, arity, &p0, &p1);
+  if (v < 0)
+    throw GError(GPUOS_EUNSUPPORTED,
+                 "expression is not one of the precompiled operators and the NVRTC path is "
+                 "not available: " + expr);
+  if (next_slot_ >= kMaxSlots) throw GError(GPUOS_EINVAL, "jump table is full (128 slots)");
+  const int slot = next_slot_++;
+  tab_.slot[slot] = SlotEntry{v, p0, p1, arity};
+  upload_tables_locked();
+  slot_of_key_.emplace(key, slot);
+  return slot;
+}
+
+int Executor::register_reduce(const std::string& key, const std::string& op_name) {
+  std::lock_guard<std::mutex> lk(mu_);
+  auto it = slot_of_key_.find(key);
+  if (it != slot_of_key_.end()) return it->second;
+  int v;
+  if (op_name == "sum") v = V_SUM;
+  else if (op_name == "mean") v = V_MEAN;
+  else throw GError(GPUOS_EINVAL, "reduce op must be 'sum' or 'mean'");
+  if (next_slot_ >= kMaxSlots) throw GError(GPUOS_EINVAL, "jump table is full (128 slots)");
+  const int slot = next_slot_++;
+  tab_.slot[slot] = SlotEntry{v, 0.f, 0.f, 1};
+  upload_tables_locked();
+  slot_of_key_.emplace(key, slot);
+  return slot;
+}
+
+void Executor::set_alias(int logical, int physical) {
+  if (logical < 0 || logical >= kMaxSlots || physical < 0 || physical >= kMaxSlots)
+    throw GError(GPUOS_EINVAL, "slot out of range");
+  std::lock_guard<std::mutex> lk(mu_);
+  tab_.alias[logical] = physical;
+  upload_tables_locked();
+}
+
+void Executor::set_slot(int slot, int variant, float p0, float p1) {
+  if (slot < 0 || slot >= kMaxSlots) throw GError(GPUOS_EINVAL, "slot out of range");
+  const bool ok = variant == V_NONE || (variant >= 0 && variant < V_NUM_EW) ||
+                  variant == V_SUM || variant == V_MEAN;
+  if (!ok) throw GError(GPUOS_EINVAL, "unknown operator id " + std::to_string(variant));
+  std::lock_guard<std::mutex> lk(mu_);
+  const int arity = (variant == V_ADD || variant == V_MUL || variant == V_SUB ||
+                     variant == V_DIV0 || variant == V_DIV || variant == V_MAX ||
+                     variant == V_MIN || variant == V_POW) ? 2 : 1;
+  tab_.slot[slot] = SlotEntry{variant, p0, p1, arity};
+  upload_tables_locked();
+}
+
+void Executor::get_slot(int slot, int* variant, float* p0, float* p1, int* alias) {
+  if (slot < 0 || slot >= kMaxSlots) throw GError(GPUOS_EINVAL, "slot out of range");
+  std::lock_guard<std::mutex> lk(mu_);
+  if (variant) *variant = tab_.slot[slot].variant;
+  if (p0) *p0 = tab_.slot[slot].p0;
+  if (p1) *p1 = tab_.slot[slot].p1;
+  if (alias) *alias = tab_.alias[slot];
+}
+
+void Executor::set_timing(bool on) {
+  std::lock_guard<std::mutex> lk(mu_);
+  timing_ = on;
+}
+
+size_t Executor::take_timings(float* ms, size_t cap) {
+  std::lock_guard<std::mutex> lk(mu_);
+  DeviceGuard g(device_);
+  size_t n = 0;
+  for (auto& pr : timed_) {
+    GCU(cudaEventSynchronize(pr.second));
+    float t = 0.f;
+    GCU(cudaEventElapsedTime(&t, pr.first, pr.second));
+    if (ms && n < cap) ms[n] = t;
+    ++n;
+    ev_pool_.push_back(pr.first);
+    ev_pool_.push_back(pr.second);
+  }
+  timed_.clear();
+  return n;
+}
+
+void Executor::set_yield_every(uint64_t every) {
+  std::lock_guard<std::mutex> lk(mu_);
+  hctrl_->yield_every = every;
+}
+
+void Executor::set_debug_level(int level) {
+  std::lock_guard<std::mutex> lk(mu_);
+  debug_level_ = level;
+  hctrl_->debug_level = (uint32_t)level;
+}
+
+void Executor::stats(gpuos_stats* out) {
+  std::lock_guard<std::mutex> lk(mu_);
+  reclaim();
+  std::memset(out, 0, sizeof(*out));
+  out->published = next_seq_;
+  out->staged = opt_.mode == GPUOS_MODE_PERSISTENT ? hctrl_->staged : next_seq_;
+  out->processed = done_wm_;
+  out->retired = retired_wm_;
+  out->heartbeat = hctrl_->heartbeat;
+  out->requests = requests_;
+  out->pending = pending_.size();
+  out->errors = errors_;
+  out->relaunches = relaunches_;
+  out->dev_ns = dev_ns_;
+  out->capacity = opt_.capacity;
+  out->max_batch = opt_.max_batch;
+  out->mode = opt_.mode;
+  out->worker_alive = 0;
+  if (opt_.mode == GPUOS_MODE_PERSISTENT && worker_launched_) {
+    DeviceGuard g(device_);
+    out->worker_alive = cudaStreamQuery(s_worker_) == cudaErrorNotReady ? 1 : 0;
+  }
+  out->quit = (int32_t)hctrl_->quit;
+  out->grid = opt_.mode == GPUOS_MODE_PERSISTENT ? grid_ : sm_count_ * batch_bps_;
+  out->block = block_;
+  out->device = device_;
+}
+
+void Executor::shutdown() {
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    if (!started_) return;
+  }
+  std::string first_error;
+  try {
+    flush(true, nullptr);
+  } catch (const std::exception& e) {
+    first_error = e.what();
+  }
+  std::lock_guard<std::mutex> lk(mu_);
+  DeviceGuard g(device_);
+  started_ = false;
+  if (worker_launched_) {
+    hctrl_->quit = 1u;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    const auto t0 = std::chrono::steady_clock::now();
+    while (cudaStreamQuery(s_worker_) == cudaErrorNotReady) {
+      const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      if (el > sync_timeout_s_ + idle_ns_ * 1e-9) break;
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    worker_launched_ = false;
+  }
+  cudaStreamSynchronize(s_own_);
+  cudaStreamSynchronize(s_ctrl_);
+  if (ring_) cudaFree(ring_);
+  if (dctrl_) cudaFree(dctrl_);
+  if (tab_dev_) cudaFree(tab_dev_);
+  if (partials_) cudaFree(partials_);
+  if (counters_) cudaFree(counters_);
+  if (arena_) cudaFreeHost(arena_);
+  if (hostblk_) cudaFreeHost(hostblk_);
+  if (last_event_) cudaEventDestroy(last_event_);
+  for (auto& pr : timed_) {
+    cudaEventDestroy(pr.first);
+    cudaEventDestroy(pr.second);
+  }
+  for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
+  timed_.clear();
+  ev_pool_.clear();
+  if (s_worker_) cudaStreamDestroy(s_worker_);
+  if (s_ctrl_) cudaStreamDestroy(s_ctrl_);
+  if (s_own_) cudaStreamDestroy(s_own_);
+  ring_ = nullptr; dctrl_ = nullptr; tab_dev_ = nullptr; partials_ = nullptr; counters_ = nullptr;
+  arena_ = nullptr; hostblk_ = nullptr; last_event_ = nullptr;
+  s_worker_ = s_ctrl_ = s_own_ = nullptr;
+  if (!first_error.empty()) throw GError(GPUOS_EDEVICE, "shutdown: " + first_error);
+}
+
+}  // namespace gpuos
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+using gpuos::Executor;
+using gpuos::GError;
+
+namespace {
+template <class F>
+int32_t guard(F&& f) {
+  try {
+    f();
+    return GPUOS_OK;
+  } catch (const GError& e) {
+    gpuos::t_last_error = e.what();
+    return e.code;
+  } catch (const std::exception& e) {
+    gpuos::t_last_error = e.what();
+    return GPUOS_EINVAL;
+  } catch (...) {
+    gpuos::t_last_error = "unknown error";
+    return GPUOS_EINVAL;
+  }
+}
+Executor* X(gpuos_executor* ex) {
+  if (!ex) throw GError(GPUOS_ESTATE, "executor handle is NULL");
+  return reinterpret_cast<Executor*>(ex);
+}
+}  // namespace
+
+extern "C" {
+
+int32_t gpuos_abi_version(void) { return GPUOS_ABI_VERSION; }
+
+const char* gpuos_last_error(void) { return gpuos::t_last_error.c_str(); }
+
+int32_t gpuos_executor_create(int32_t device, const gpuos_options* opt, gpuos_executor** out) {
+  return guard([&] {
+    if (!out) throw GError(GPUOS_EINVAL, "out is NULL");
+    gpuos_options o;
+    std::memset(&o, 0, sizeof(o));
+    if (opt) o = *opt;
+    *out = reinterpret_cast<gpuos_executor*>(new Executor(device, o));
+  });
+}
+
+int32_t gpuos_executor_destroy(gpuos_executor* ex) {
+  return guard([&] {
+    Executor* e = X(ex);
+    std::unique_ptr<Executor> hold(e);
+    e->shutdown();
+  });
+}
+
+int32_t gpuos_submit_builtin(gpuos_executor* ex, int32_t op, const gpuos_tensor* a,
+                             const gpuos_tensor* b, const gpuos_tensor* out) {
+  return guard([&] {
+    if (op < 0 || op > 3) throw GError(GPUOS_EINVAL, "builtin op must be 0..3 (add, mul, sub, div)");
+    if (!a || !b || !out) throw GError(GPUOS_EINVAL, "a, b and out are required");
+    X(ex)->submit_ew(op, false, 0.f, 0.f, a, b, *out);
+  });
+}
+
+int32_t gpuos_submit_unary(gpuos_executor* ex, int32_t slot, const gpuos_tensor* a,
+                           const gpuos_tensor* out) {
+  return guard([&] {
+    if (!a || !out) throw GError(GPUOS_EINVAL, "a and out are required");
+    if (slot < 0 || slot >= gpuos::kMaxSlots) throw GError(GPUOS_EINVAL, "slot out of range");
+    X(ex)->submit_ew(slot, true, 0.f, 0.f, a, nullptr, *out);
+  });
+}
+
+int32_t gpuos_submit_binary(gpuos_executor* ex, int32_t slot, const gpuos_tensor* a,
+                            const gpuos_tensor* b, const gpuos_tensor* out) {
+  return guard([&] {
+    if (!a || !b || !out) throw GError(GPUOS_EINVAL, "a, b and out are required");
+    if (slot < 0 || slot >= gpuos::kMaxSlots) throw GError(GPUOS_EINVAL, "slot out of range");
+    X(ex)->submit_ew(slot, true, 0.f, 0.f, a, b, *out);
+  });
+}
+
+int32_t gpuos_register_elementwise(gpuos_executor* ex, const char* key, const char* expr,
+                                   int32_t arity, int32_t* slot_out) {
+  return guard([&] {
+    if (!key || !expr || !slot_out) throw GError(GPUOS_EINVAL, "key, expr and slot_out are required");
+    *slot_out = X(ex)->register_elementwise(key, expr, arity);
+  });
+}
+
+int32_t gpuos_register_reduce(gpuos_executor* ex, const char* key, const char* op_name,
+                              int32_t* slot_out) {
+  return guard([&] {
+    if (!key || !op_name || !slot_out) throw GError(GPUOS_EINVAL, "key, op_name and slot_out are required");
+    *slot_out = X(ex)->register_reduce(key, op_name);
+  });
+}
+
+int32_t gpuos_submit_reduce(gpuos_executor* ex, int32_t slot, const gpuos_tensor* x,
+                            const gpuos_tensor* out, const int32_t* axes, int32_t naxes,
+                            int32_t keepdim) {
+  return guard([&] {
+    if (!x || !out) throw GError(GPUOS_EINVAL, "x and out are required");
+    if (naxes < 0 || naxes > 8 || (naxes > 0 && !axes)) throw GError(GPUOS_EINVAL, "bad axes");
+    if (slot < 0 || slot >= gpuos::kMaxSlots) throw GError(GPUOS_EINVAL, "slot out of range");
+    X(ex)->submit_reduce(slot, true, *x, *out, axes, naxes, keepdim != 0);
+  });
+}
+
+int32_t gpuos_submit_task(gpuos_executor* ex, const void* task) {
+  return guard([&] {
+    if (!task) throw GError(GPUOS_EINVAL, "task is NULL");
+    X(ex)->submit_task(task);
+  });
+}
+
+int32_t gpuos_flush(gpuos_executor* ex, int32_t sync, void* stream, uint64_t* ticket_out) {
+  return guard([&] {
+    const uint64_t t = X(ex)->flush(sync != 0, static_cast<cudaStream_t>(stream));
+    if (ticket_out) *ticket_out = t;
+  });
+}
+
+int32_t gpuos_wait(gpuos_executor* ex, uint64_t ticket, double timeout_s) {
+  return guard([&] { X(ex)->wait(ticket, timeout_s); });
+}
+
+int32_t gpuos_set_alias(gpuos_executor* ex, int32_t logical, int32_t physical) {
+  return guard([&] { X(ex)->set_alias(logical, physical); });
+}
+
+int32_t gpuos_set_slot(gpuos_executor* ex, int32_t slot, int32_t variant, float p0, float p1) {
+  return guard([&] { X(ex)->set_slot(slot, variant, p0, p1); });
+}
+
+int32_t gpuos_get_slot(gpuos_executor* ex, int32_t slot, int32_t* variant, float* p0, float* p1,
+                       int32_t* alias) {
+  return guard([&] {
+    int v = 0, al = 0;
+    X(ex)->get_slot(slot, &v, p0, p1, &al);
+    if (variant) *variant = v;
+    if (alias) *alias = al;
+  });
+}
+
+int32_t gpuos_variant_by_name(const char* name) {
+  return name ? gpuos::variant_by_name(name) : -1;
+}
+
+int32_t gpuos_set_timing(gpuos_executor* ex, int32_t on) {
+  return guard([&] { X(ex)->set_timing(on != 0); });
+}
+
+int32_t gpuos_take_timings(gpuos_executor* ex, float* ms, uint64_t cap, uint64_t* n_out) {
+  return guard([&] {
+    const size_t n = X(ex)->take_timings(ms, (size_t)cap);
+    if (n_out) *n_out = n;
+  });
+}
+
+int32_t gpuos_set_yield_every(gpuos_executor* ex, uint64_t every) {
+  return guard([&] { X(ex)->set_yield_every(every); });
+}
+
+int32_t gpuos_set_debug_level(gpuos_executor* ex, int32_t level) {
+  return guard([&] { X(ex)->set_debug_level(level); });
+}
+
+int32_t gpuos_worker_alive(gpuos_executor* ex) {
+  int32_t alive = 0;
+  int32_t rc = guard([&] { alive = X(ex)->worker_alive() ? 1 : 0; });
+  return rc < 0 ? rc : alive;
+}
+
+int32_t gpuos_plan_elementwise(int32_t variant, float p0, float p1, const gpuos_tensor* a,
+                               const gpuos_tensor* b, const gpuos_tensor* out, gpuos_plan* plan) {
+  return guard([&] {
+    if (!a || !out || !plan) throw GError(GPUOS_EINVAL, "a, out and plan are required");
+    gpuos::Pending p;
+    gpuos::build_ew(p, variant, false, p0, p1, a, b, *out);
+    std::memcpy(plan->record, &p.r, sizeof(p.r));
+    plan->nchunk = p.nchunk;
+    plan->has_ext = p.has_ext ? 1u : 0u;
+    plan->partials = p.partials;
+    plan->counters = p.counters;
+  });
+}
+
+int32_t gpuos_plan_reduce(int32_t variant, const gpuos_tensor* x, const gpuos_tensor* out,
+                          const int32_t* axes, int32_t naxes, int32_t keepdim, gpuos_plan* plan) {
+  return guard([&] {
+    if (!x || !out || !plan) throw GError(GPUOS_EINVAL, "x, out and plan are required");
+    if (naxes < 0 || naxes > 8 || (naxes > 0 && !axes)) throw GError(GPUOS_EINVAL, "bad axes");
+    gpuos::Pending p;
+    gpuos::build_reduce(p, variant, false, *x, *out, axes, naxes, keepdim != 0);
+    std::memcpy(plan->record, &p.r, sizeof(p.r));
+    plan->nchunk = p.nchunk;
+    plan->has_ext = p.has_ext ? 1u : 0u;
+    plan->partials = p.partials;
+    plan->counters = p.counters;
+  });
+}
+
+int32_t gpuos_match_expression(const char* expr, int32_t arity, int32_t* variant, float* p0,
+                               float* p1) {
+  return guard([&] {
+    if (!expr || !variant) throw GError(GPUOS_EINVAL, "expr and variant are required");
+    float a = 0.f, b = 0.f;
+    *variant = gpuos::match_builtin_expr(expr, arity, &a, &b);
+    if (p0) *p0 = a;
+    if (p1) *p1 = b;
+  });
+}
+
+int32_t gpuos_get_stats(gpuos_executor* ex, gpuos_stats* out) {
+  return guard([&] {
+    if (!out) throw GError(GPUOS_EINVAL, "out is NULL");
+    X(ex)->stats(out);
+  });
+}
+
+}  // extern "C"

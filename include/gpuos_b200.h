@@ -1,0 +1,220 @@
+/* gpuos_b200.h — C ABI of the B200 aggregated small-op executor.
+ *
+ * Plain C types only (no torch, no C++): a caller that cannot link C++ (cgo,
+ * JNI, ctypes, N-API) binds these symbols directly.  Every entry point
+ * returns a status (0 = success, negative = error; gpuos_last_error() gives
+ * the message of the calling thread's last failure) instead of terminating
+ * the process the way the reference does (pytorch_ext/gpuos_ext.cpp:32-58).
+ *
+ * Each declaration names the reference interface it replaces.  Reference
+ * paths are relative to the Multi-V-VM/GPUOS repository.
+ */
+#ifndef GPUOS_B200_H
+#define GPUOS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GPUOS_ABI_VERSION 1
+
+/* status codes */
+#define GPUOS_OK 0
+#define GPUOS_EINVAL (-1)       /* bad argument (shape, dtype, slot, ...) */
+#define GPUOS_ECUDA (-2)        /* CUDA runtime / driver error */
+#define GPUOS_ETIMEOUT (-3)     /* a bounded wait expired */
+#define GPUOS_ESTATE (-4)       /* executor not initialised / shut down */
+#define GPUOS_EUNSUPPORTED (-5) /* feature not available (e.g. JIT without NVRTC) */
+#define GPUOS_EDEVICE (-6)      /* a batch reported an error on the device */
+#define GPUOS_ENVRTC (-7)       /* NVRTC compilation failed */
+
+/* dtype codes: the reference's DType enum (src/common.h:14-20) */
+#define GPUOS_F32 0
+#define GPUOS_F16 1
+#define GPUOS_BF16 2
+
+/* execution modes */
+#define GPUOS_MODE_PERSISTENT 0 /* resident worker grid fed through a mapped doorbell */
+#define GPUOS_MODE_STREAM 1     /* one kernel per batch on the caller's CUDA stream */
+
+/* builtin operator codes accepted by gpuos_submit_builtin: the op codes of the
+ * reference's op_batch switch (src/persistent_kernel.cu:101-106) */
+#define GPUOS_OP_ADD 0
+#define GPUOS_OP_MUL 1
+#define GPUOS_OP_SUB 2
+#define GPUOS_OP_DIV 3 /* B == 0 gives 0, as op_batch does */
+
+/* A strided tensor view: element strides, up to 8 dims.  Same layout as the
+ * reference's TensorRef (src/common.h:25-31). */
+typedef struct gpuos_tensor {
+  void* data;
+  int32_t dtype;
+  int32_t ndim;
+  int64_t sizes[8];
+  int64_t strides[8];
+} gpuos_tensor;
+
+typedef struct gpuos_executor gpuos_executor;
+
+typedef struct gpuos_options {
+  int32_t capacity;          /* queue capacity in requests; sizes the staging arena
+                                (reference: init(capacity), gpuos_ext.cpp:328-339) */
+  int32_t threads_per_block; /* worker CTA size (reference default 256, gpuos_ext.cpp:863) */
+  int32_t mode;              /* GPUOS_MODE_* */
+  int32_t blocks_per_sm;     /* 0 = from the occupancy calculator */
+  double idle_ms;            /* persistent worker exits after this long idle (0 = default) */
+  double sync_timeout_s;     /* bound on every host wait (0 = default) */
+  int32_t max_batch;         /* requests per batch (reference GPUOS_BATCH_SHARD, default 512) */
+  int32_t reserved[7];
+} gpuos_options;
+
+typedef struct gpuos_stats {
+  uint64_t published;   /* batches published (reference: tail) */
+  uint64_t staged;      /* batches staged on the device (reference: head) */
+  uint64_t processed;   /* batches completed */
+  uint64_t retired;     /* batches whose staging memory was reclaimed */
+  uint64_t heartbeat;   /* idle polls of the worker's ingest CTA (reference g_heartbeat) */
+  uint64_t requests;    /* requests submitted */
+  uint64_t pending;     /* requests waiting for the next flush */
+  uint64_t errors;      /* device-reported request errors */
+  uint64_t relaunches;  /* persistent worker launches */
+  uint64_t dev_ns;      /* device time of completed batches (first claim -> last chunk) */
+  int32_t capacity;
+  int32_t max_batch;
+  int32_t mode;
+  int32_t worker_alive;
+  int32_t quit;
+  int32_t grid;
+  int32_t block;
+  int32_t device;
+} gpuos_stats;
+
+/* ABI version (reference: abi_version() -> 1, gpuos_ext.cpp:865). */
+int32_t gpuos_abi_version(void);
+
+/* Message of the calling thread's last failed call. */
+const char* gpuos_last_error(void);
+
+/* Create one executor on `device` (replaces init(): gpuos_ext.cpp:328-382 and
+ * launch_init_builtin_ops / launch_persistent_worker, persistent_kernel.cu:203-213).
+ * opt may be NULL for defaults. */
+int32_t gpuos_executor_create(int32_t device, const gpuos_options* opt, gpuos_executor** out);
+
+/* Drain every published batch, stop the worker, free everything
+ * (replaces shutdown(): gpuos_ext.cpp:384-421). */
+int32_t gpuos_executor_destroy(gpuos_executor* ex);
+
+/* Queue out = a <op> b with op in GPUOS_OP_* (replaces submit_add / submit_mul /
+ * submit_sub / submit_div: gpuos_ext.cpp:459-493).  Broadcasting follows
+ * torch: right-aligned, size-1 dims repeat. */
+int32_t gpuos_submit_builtin(gpuos_executor* ex, int32_t op, const gpuos_tensor* a,
+                             const gpuos_tensor* b, const gpuos_tensor* out);
+
+/* Queue a request through jump-table slot `slot` (replaces submit_unary /
+ * submit_binary: gpuos_ext.cpp:695-707).  The slot is resolved on the device
+ * when the batch runs, so a hot swap affects every batch that starts after it. */
+int32_t gpuos_submit_unary(gpuos_executor* ex, int32_t slot, const gpuos_tensor* a,
+                           const gpuos_tensor* out);
+int32_t gpuos_submit_binary(gpuos_executor* ex, int32_t slot, const gpuos_tensor* a,
+                            const gpuos_tensor* b, const gpuos_tensor* out);
+
+/* Register an fp32 expression over A (and B) and return its slot (replaces
+ * register_elementwise: gpuos_ext.cpp:681-692).  The expressions the
+ * reference scheduler emits map onto precompiled operators; any other
+ * expression is compiled with NVRTC for sm_100a. */
+int32_t gpuos_register_elementwise(gpuos_executor* ex, const char* key, const char* expr,
+                                   int32_t arity, int32_t* slot_out);
+
+/* Register "sum" or "mean" and return its slot (replaces register_reduce:
+ * gpuos_ext.cpp:814-825, 847-849). */
+int32_t gpuos_register_reduce(gpuos_executor* ex, const char* key, const char* op_name,
+                              int32_t* slot_out);
+
+/* Queue a sum/mean of x over `axes` into out (replaces submit_reduce:
+ * gpuos_ext.cpp:827-856). */
+int32_t gpuos_submit_reduce(gpuos_executor* ex, int32_t slot, const gpuos_tensor* x,
+                            const gpuos_tensor* out, const int32_t* axes, int32_t naxes,
+                            int32_t keepdim);
+
+/* Queue one request given in the reference's 496-byte Task layout
+ * (src/common.h:34-46): op is a jump-table slot, in0/in1/out0 are TensorRefs
+ * whose sizes/strides are already aligned to the output. */
+int32_t gpuos_submit_task(gpuos_executor* ex, const void* task);
+
+/* Publish every queued request as one or more batches.  `stream` is the
+ * cudaStream_t the inputs were produced on (NULL: the executor's stream).  In
+ * stream mode the batches run on that stream; in persistent mode the host
+ * waits for that stream before ringing the doorbell.  With sync != 0 the call
+ * returns after the batches are done (replaces flush(sync):
+ * gpuos_ext.cpp:496-622; the wait is bounded and polls mapped memory
+ * instead of sleeping 5 ms between device reads). *ticket_out (optional)
+ * receives a ticket for gpuos_wait. */
+int32_t gpuos_flush(gpuos_executor* ex, int32_t sync, void* stream, uint64_t* ticket_out);
+
+/* Wait until every batch published before `ticket` is done. */
+int32_t gpuos_wait(gpuos_executor* ex, uint64_t ticket, double timeout_s);
+
+/* Dual-slot hot swap: route logical slot to physical slot (replaces
+ * gpu_set_alias_async, persistent_kernel.cu:224-226). */
+int32_t gpuos_set_alias(gpuos_executor* ex, int32_t logical, int32_t physical);
+
+/* Online hot swap: overwrite what a physical slot runs (replaces
+ * gpu_set_op_table_async, persistent_kernel.cu:220-222; takes an operator
+ * id instead of a raw device function pointer). */
+int32_t gpuos_set_slot(gpuos_executor* ex, int32_t slot, int32_t variant, float p0, float p1);
+
+/* Read a slot (variant id, parameters) and the alias of a logical slot. */
+int32_t gpuos_get_slot(gpuos_executor* ex, int32_t slot, int32_t* variant, float* p0, float* p1,
+                       int32_t* alias);
+
+/* Operator id of a builtin by name ("add", "gelu", "sum", ...), or -1. */
+int32_t gpuos_variant_by_name(const char* name);
+
+/* Per-launch timing of the batch kernel in stream mode: with timing on, a
+ * CUDA event pair brackets every launch; gpuos_take_timings waits for them,
+ * writes up to `cap` durations in milliseconds and returns the count in
+ * *n_out.  (No counterpart in the reference, which has no kernel timing.) */
+int32_t gpuos_set_timing(gpuos_executor* ex, int32_t on);
+int32_t gpuos_take_timings(gpuos_executor* ex, float* ms, uint64_t cap, uint64_t* n_out);
+
+/* Worker control (replaces gpu_set_yield_every_async / gpu_set_debug_level_async,
+ * persistent_kernel.cu:232-238, and worker_alive(), gpuos_ext.cpp:128-135). */
+int32_t gpuos_set_yield_every(gpuos_executor* ex, uint64_t every);
+int32_t gpuos_set_debug_level(gpuos_executor* ex, int32_t level);
+int32_t gpuos_worker_alive(gpuos_executor* ex);
+
+/* How the executor lays out one request, without running it (no GPU
+ * needed): the 128-byte request record (layout: gpuos_b200/csrc/gpuos_abi.h,
+ * struct Req), its chunk count and scratch needs.  Planning is the host half
+ * of build_binary_task / build_reduce_task (gpuos_ext.cpp:167-201, 827-845). */
+typedef struct gpuos_plan {
+  uint8_t record[128];
+  uint32_t nchunk;
+  uint32_t has_ext;
+  uint64_t partials; /* floats of reduction scratch */
+  uint64_t counters; /* combine counters */
+} gpuos_plan;
+
+int32_t gpuos_plan_elementwise(int32_t variant, float p0, float p1, const gpuos_tensor* a,
+                               const gpuos_tensor* b, const gpuos_tensor* out, gpuos_plan* plan);
+int32_t gpuos_plan_reduce(int32_t variant, const gpuos_tensor* x, const gpuos_tensor* out,
+                          const int32_t* axes, int32_t naxes, int32_t keepdim, gpuos_plan* plan);
+
+/* Which precompiled operator (and parameters) an expression string of the
+ * reference scheduler maps to; *variant = -1 when it needs NVRTC. */
+int32_t gpuos_match_expression(const char* expr, int32_t arity, int32_t* variant, float* p0,
+                               float* p1);
+
+/* Counters (replaces peek_queue(), gpuos_ext.cpp:435-456, and
+ * gpu_get_processed_count_async / gpu_get_heartbeat_async,
+ * persistent_kernel.cu:216-230). */
+int32_t gpuos_get_stats(gpuos_executor* ex, gpuos_stats* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPUOS_B200_H */

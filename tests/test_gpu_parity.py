@@ -1,0 +1,550 @@
+"""Parity of the CUDA path with the CPU oracle (needs a GPU: -m gpu).
+
+Every test builds its inputs on the CPU from a fixed seed, runs the oracle on
+the CPU copies and the executor on device copies of the same bytes, and
+compares.  Tolerances (tests/tolerance.py): bit-exact for the exact
+operators and casts; documented CUDA ulp bounds, propagated through the
+formula, for transcendentals; 1e-5 * sum|x| for fp32 sum/mean.
+"""
+import ctypes
+import hashlib
+import json
+import time
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import gpuos_b200
+import gpuos_b200.cabi as C
+import oracle
+from gpuos_b200 import workloads as W
+from tolerance import EXACT, RED_REL, check_transcendental
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+KAT = json.loads((Path(__file__).parent / "golden" / "kat.json").read_text())
+MODES = [C.MODE_PERSISTENT, C.MODE_STREAM]
+MODE_IDS = ["persistent", "stream"]
+PARAMS = {"leaky_relu": (0.01, 0.0), "clamp": (-0.5, 0.5), "elu": (1.0, 0.0),
+          "softplus": (1.0, 0.0), "clamp_min": (-0.25, 0.0), "clamp_max": (0.25, 0.0)}
+ALL_OPS = [n for n, v in sorted(oracle.VARIANTS.items(), key=lambda x: x[1]) if v < 32]
+
+
+@pytest.fixture(params=MODES, ids=MODE_IDS)
+def ex(request):
+    e = C.Executor(0, mode=request.param)
+    yield e
+    e.close()
+
+
+@pytest.fixture(params=["persistent", "stream"])
+def ext(request):
+    g = gpuos_b200.load()
+    g.init(4096, 256, mode=request.param)
+    yield g
+    g.shutdown()
+
+
+def gpu(t):
+    return t.to(DEV)
+
+
+def slot_of(e, op):
+    """A jump-table slot running operator `op` (registered through the
+    reference scheduler's expression string where there is one)."""
+    if op in W.EXPR:
+        expr, ar = W.EXPR[op]
+        return e.register_elementwise(f"t|{op}", expr, ar)
+    if op in PARAMS:
+        expr, key = W.param_expr(op, *PARAMS[op])
+        return e.register_elementwise(key, expr, 1)
+    s = e.register_elementwise(f"t|{op}|slot", "(A)", 1)
+    e.set_slot(s, C.variant(op), *PARAMS.get(op, (0.0, 0.0)))
+    return s
+
+
+def _bits(t):
+    return t.view(torch.int32 if t.dtype == torch.float32 else torch.int16)
+
+
+def compare(op, a, b, got, p0=0.0, p1=0.0, where=""):
+    """got: CPU tensor read back from the GPU; checks it against the oracle.
+    Exact operators: bit for bit.  Transcendentals: fp32 results within the
+    propagated CUDA ulp bound of the exact value; 16-bit results within one
+    output ulp of the oracle's fp32-then-rounded value."""
+    ref = torch.empty_like(got)
+    oracle.ew(op, a, b, ref, p0, p1)
+    if op in EXACT:
+        if not torch.equal(_bits(got), _bits(ref)):
+            bad = (_bits(got) != _bits(ref)).nonzero()[:5].tolist()
+            raise AssertionError(f"{op}{where}: bit mismatch at {bad}")
+        return
+    if got.dtype != torch.float32:
+        diff = (got.double() - ref.double()).abs()
+        rel = 2 ** -7 if got.dtype == torch.bfloat16 else 2 ** -10
+        step = (ref.double().abs() * rel).clamp_min(1e-30)
+        assert bool((diff <= step * 1.01).all()), f"{op}{where}: more than 1 output ulp off"
+        return
+    ex64 = torch.empty(got.shape, dtype=torch.float64)
+    oracle.ew(op, a, b, ex64, p0, p1, exact=True)
+    A = torch.broadcast_to(a.float(), got.shape).reshape(-1).numpy()
+    B = (torch.broadcast_to(b.float(), got.shape).reshape(-1).numpy() if b is not None
+         else np.zeros(got.numel()))
+    ok, worst, i = check_transcendental(op, A, B, got.reshape(-1).numpy(),
+                                        ex64.reshape(-1).numpy(), p0, p1)
+    assert ok, f"{op}{where}: error {worst:.2f}x the bound at flat index {i} (A={A[i]})"
+
+
+# --------------------------------------------------------------------------
+# the reference's own test vectors
+# --------------------------------------------------------------------------
+def kat_inputs(k):
+    i = torch.arange(k["n"], dtype=torch.float32)
+    a = torch.tensor(np.float32(k["a"][0])) * i
+    b = np.float32(k["b"][0]) + (torch.arange(k["n"]) % k["b"][1]).float()
+    return a, b
+
+
+@pytest.mark.parametrize("name", ["host_mul", "online_add", "online_mul", "dual_add", "dual_mul"])
+def test_reference_vectors(ex, name):
+    k = KAT[name]
+    a, b = kat_inputs(k)
+    ga, gb = gpu(a), gpu(b)
+    out = torch.full_like(ga, float("nan"))
+    ex.builtin({"add": C.OP_ADD, "mul": C.OP_MUL}[k["op"]], ga, gb, out)
+    ex.flush(sync=True)
+    got = out.cpu().numpy()
+    assert [int(x) for x in got[:16].view(np.uint32)] == k["head_bits"]
+    assert hashlib.sha256(got.tobytes()).hexdigest() == k["sha256"]
+
+
+def test_dual_slot_switch(ex):
+    """test/dual_slot_switch.cpp: logical slot 0 runs add, is routed to a
+    mul in another physical slot, then rolled back."""
+    a, b = kat_inputs(KAT["dual_add"])
+    ga, gb = gpu(a), gpu(b)
+    outs = [torch.empty_like(ga) for _ in range(3)]
+    ex.binary(0, ga, gb, outs[0])
+    ex.flush(sync=True)
+    s = ex.register_elementwise("op_mul", "(A * B)", 2)
+    ex.set_alias(0, s)
+    ex.binary(0, ga, gb, outs[1])
+    ex.flush(sync=True)
+    ex.set_alias(0, 0)
+    ex.binary(0, ga, gb, outs[2])
+    ex.flush(sync=True)
+    for o, name in zip(outs, ["dual_add", "dual_mul", "dual_add"]):
+        got = o.cpu().numpy()
+        assert hashlib.sha256(got.tobytes()).hexdigest() == KAT[name]["sha256"], name
+
+
+def test_online_switch(ex):
+    """test/online_switch.cpp: slot 0 is overwritten in place (add -> mul)."""
+    a, b = kat_inputs(KAT["online_add"])
+    ga, gb = gpu(a), gpu(b)
+    c_add, c_mul = torch.empty_like(ga), torch.empty_like(ga)
+    ex.binary(0, ga, gb, c_add)
+    ex.flush(sync=True)
+    ex.set_slot(0, C.variant("mul"))
+    ex.binary(0, ga, gb, c_mul)
+    ex.flush(sync=True)
+    ex.set_slot(0, C.variant("add"))
+    assert hashlib.sha256(c_add.cpu().numpy().tobytes()).hexdigest() == KAT["online_add"]["sha256"]
+    assert hashlib.sha256(c_mul.cpu().numpy().tobytes()).hexdigest() == KAT["online_mul"]["sha256"]
+
+
+def test_reference_task_layout(ex):
+    """A request in the reference's 496-byte Task layout (src/common.h:34-46)."""
+    n = 1000
+    a, b = torch.randn(n), torch.randn(n)
+    ga, gb, go = gpu(a), gpu(b), torch.empty(n, device=DEV)
+    raw = bytearray(496)
+
+    def tref(off, t):
+        d = C.tensor(t)
+        raw[off:off + 144] = bytes(d)
+
+    raw[0:4] = (1).to_bytes(4, "little")        # op: jump-table slot 1 (mul)
+    raw[8:12] = (1).to_bytes(4, "little")       # ndim
+    raw[16:24] = n.to_bytes(8, "little")        # numel
+    tref(64, ga)
+    tref(208, gb)
+    tref(352, go)
+    ex.task(bytes(raw))
+    ex.flush(sync=True)
+    assert torch.equal(go.cpu(), a * b)
+
+
+# --------------------------------------------------------------------------
+# every operator, ragged sizes, aligned and misaligned views
+# --------------------------------------------------------------------------
+SIZES = [1, 7, 255, 256, 257, 1000, 4097, 33000]
+
+
+@pytest.mark.parametrize("op", ALL_OPS)
+def test_every_operator(op):
+    """Every operator on ragged sizes; shift=1 starts the views one element
+    into their buffers, so the 16-byte vector path is off and the scalar
+    path runs."""
+    with C.Executor(0, mode=C.MODE_STREAM) as e:
+        s = slot_of(e, op)
+        g = torch.Generator().manual_seed(100 + ALL_OPS.index(op))
+        binary = op in oracle.BINARY
+        cases = []
+        for n in SIZES:
+            for shift in (0, 1):
+                af = torch.randn(n + shift, generator=g)
+                bf = torch.randn(n + shift, generator=g)
+                if op in ("log", "sqrt", "pow"):
+                    af = af.abs() + 1e-3
+                if op == "pow":
+                    bf = torch.rand(n + shift, generator=g) * 1.5 + 0.5
+                if op in ("div", "div0"):
+                    bf = torch.sign(bf) * (bf.abs() + 0.1)
+                a, b = af[shift:], bf[shift:]
+                ga, gb = gpu(af)[shift:], gpu(bf)[shift:]
+                go = torch.empty(n + shift, device=DEV)[shift:]
+                if binary:
+                    e.binary(s, ga, gb, go)
+                else:
+                    e.unary(s, ga, go)
+                cases.append((a, b if binary else None, go, n, shift))
+        e.flush(sync=True)
+        p0, p1 = PARAMS.get(op, (0.0, 0.0))
+        for a, b, go, n, shift in cases:
+            compare(op, a, b, go.cpu(), p0, p1, where=f" n={n} shift={shift}")
+
+
+@pytest.mark.parametrize("op", ["add", "mul", "div0", "maximum", "copy", "relu", "clamp"])
+@pytest.mark.parametrize("dts", [("f16", "f32", "f32"), ("bf16", "bf16", "bf16"),
+                                 ("f16", "f16", "f16"), ("f32", "f32", "bf16"),
+                                 ("f32", "f32", "f16")])
+def test_dtype_casts_bit_exact(op, dts):
+    D = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+    da, db, do = (D[x] for x in dts)
+    g = torch.Generator().manual_seed(7)
+    with C.Executor(0, mode=C.MODE_PERSISTENT) as e:
+        s = slot_of(e, op)
+        cases = []
+        for n in (33, 4096, 5003):
+            a = (torch.randn(n, generator=g) * 3).to(da)
+            b = (torch.randn(n, generator=g) * 3).to(db)
+            if op == "div0":
+                b[::7] = 0
+            go = torch.empty(n, dtype=do, device=DEV)
+            if op in oracle.BINARY:
+                e.binary(s, gpu(a), gpu(b), go)
+            else:
+                e.unary(s, gpu(a), go)
+            cases.append((a, b if op in oracle.BINARY else None, go))
+        e.flush(sync=True)
+        for a, b, go in cases:
+            ref = torch.empty(go.shape, dtype=do)
+            oracle.ew(op, a, b, ref, *PARAMS.get(op, (0.0, 0.0)))
+            got = go.cpu()
+            assert torch.equal(got.view(torch.int16 if do != torch.float32 else torch.int32),
+                               ref.view(torch.int16 if do != torch.float32 else torch.int32)), (op, dts)
+
+
+# --------------------------------------------------------------------------
+# broadcast, views, strided layouts
+# --------------------------------------------------------------------------
+def run_one(e, op, a, b, out_shape, out_dtype=torch.float32, out=None, p=(0.0, 0.0)):
+    s = slot_of(e, op)
+    ga = gpu(a)
+    gb = gpu(b) if b is not None else None
+    go = out if out is not None else torch.empty(out_shape, dtype=out_dtype, device=DEV)
+    if b is not None:
+        e.binary(s, ga, gb, go)
+    else:
+        e.unary(s, ga, go)
+    return go
+
+
+def test_broadcast_layouts(ex):
+    g = torch.Generator().manual_seed(8)
+    B, N = 13, 520
+    a = torch.randn(B, N, generator=g)
+    row = torch.randn(N, generator=g)
+    col = torch.randn(B, 1, generator=g)
+    at = torch.randn(N, B, generator=g).t()
+    sc = torch.randn((), generator=g)
+    cases = [("add", a, row), ("mul", a, col), ("sub", at, row), ("maximum", at, col),
+             ("mul", a, sc), ("div", sc, a), ("add", row, col), ("minimum", at, at)]
+    outs = []
+    for op, x, y in cases:
+        shape = torch.broadcast_shapes(x.shape, y.shape)
+        outs.append((op, x, y, run_one(ex, op, x, y, shape)))
+    ex.flush(sync=True)
+    for op, x, y, go in outs:
+        compare(op, x, y, go.cpu(), where=f" {tuple(x.shape)}x{tuple(y.shape)}")
+
+
+def test_column_broadcast_is_torch_semantics(ex):
+    """[B,N] op [B,1] follows torch (the reference's decomposition gives the
+    wrong rows here; the oracle's reference mode reproduces that)."""
+    k = KAT["bcast_col"]
+    a = torch.tensor(k["a"])
+    c = torch.tensor(k["c"]).reshape(-1, 1)
+    go = torch.empty(a.shape, device=DEV)
+    ex.builtin(C.OP_ADD, gpu(a), gpu(c), go)
+    ex.flush(sync=True)
+    assert go.cpu().tolist() == k["torch"]
+    assert go.cpu().tolist() != k["reference"]
+
+
+def test_strided_and_noncontiguous_out(ex):
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(4, 5, 6, 7, generator=g).permute(2, 0, 3, 1)   # 4-D, no collapse
+    y = torch.randn(6, 1, 7, 1, generator=g)
+    base_out = torch.empty(6, 4, 7, 5 * 2, device=DEV)
+    go = base_out[..., ::2]                                           # strided output
+    s = slot_of(ex, "mul")
+    ex.binary(s, gpu(x), gpu(y), go)
+    ex.flush(sync=True)
+    ref = torch.empty(6, 4, 7, 5)
+    oracle.ew("mul", x, y, ref)
+    assert torch.equal(go.cpu(), ref)
+
+
+def test_broadcast_stream(ext):
+    st = W.broadcast_mixed(n_req=384, seed=1)
+    din, dout = st.device_buffers(DEV)
+    views = st.views(din, dout)
+    calls = W.Submitter(ext).prepare(st, views)
+    for i, (fn, args) in enumerate(calls):
+        fn(*args)
+        if (i + 1) % st.flush_every == 0:
+            ext.flush(sync=False)
+    ext.flush(sync=True)
+    host_out = dout.cpu()
+    for r in st.requests:
+        a, b, o = r.a.view(st.host_in), r.b.view(st.host_in), r.out.view(host_out)
+        ref = torch.empty(o.shape, dtype=o.dtype)
+        oracle.ew(r.op, a, b, ref)
+        assert torch.equal(o.view(torch.int16 if o.dtype != torch.float32 else torch.int32),
+                           ref.view(torch.int16 if o.dtype != torch.float32 else torch.int32)), r
+
+
+# --------------------------------------------------------------------------
+# whole streams through the reference-facing Python API
+# --------------------------------------------------------------------------
+def run_stream(ext, st):
+    din, dout = st.device_buffers(DEV)
+    calls = W.Submitter(ext).prepare(st, st.views(din, dout))
+    for i, (fn, args) in enumerate(calls):
+        fn(*args)
+        if (i + 1) % st.flush_every == 0:
+            ext.flush(sync=False)
+    ext.flush(sync=True)
+    return dout.cpu()
+
+
+def test_micro_add_mul_stream(ext):
+    st = W.micro_add_mul(n_req=256)
+    host_out = run_stream(ext, st)
+    for r in st.requests:
+        ref = torch.empty(r.out.shape)
+        oracle.ew(r.op, r.a.view(st.host_in), r.b.view(st.host_in), ref)
+        assert torch.equal(r.out.view(host_out), ref)
+
+
+def test_mixed_stream(ext):
+    st = W.mixed_24op(n_req=1024, seed=3)
+    host_out = run_stream(ext, st)
+    for r in st.requests:
+        a = r.a.view(st.host_in)
+        b = r.b.view(st.host_in) if r.b is not None else None
+        compare(r.op, a, b, r.out.view(host_out).clone(), r.p0, r.p1, where=f" {r.stream_op}")
+
+
+# --------------------------------------------------------------------------
+# reductions
+# --------------------------------------------------------------------------
+def check_reduce(op, x, got, axes, keepdim):
+    ref = torch.empty(got.shape, dtype=got.dtype)
+    oracle.reduce(op, x, ref, axes, keepdim)
+    cnt = 1
+    for a in axes:
+        cnt *= x.shape[a]
+    if cnt == 0:  # empty reduction: sum 0, mean NaN (torch semantics)
+        if op == "mean":
+            assert bool(got.isnan().all())
+        else:
+            assert bool((got == 0).all())
+        return
+    ex64 = x.double().sum(dim=list(axes), keepdim=keepdim)
+    mag = x.double().abs().sum(dim=list(axes), keepdim=keepdim)
+    if op == "mean":
+        ex64, mag = ex64 / cnt, mag / cnt
+    tol = RED_REL * mag + 1e-30
+    if got.dtype != torch.float32:
+        tol = tol + ex64.abs() * 2 ** -7
+    err = (got.double() - ex64).abs()
+    assert bool((err <= tol).all()), f"{op} {tuple(x.shape)} axes={axes}: max err/tol " \
+                                     f"{float((err / tol).max()):.2f}"
+    # the oracle (reference order) sits inside the same bound
+    assert bool(((ref.double() - ex64).abs() <= tol).all())
+
+
+RED_CASES = [((64, 1000), (1,), False), ((3, 8191), (-1,), True), ((5, 9000), (1,), False),
+             ((2, 40000), (1,), True), ((300, 70), (1,), False), ((1, 64), (1,), False),
+             ((4096, 3), (1,), True), ((8, 16, 32), (0, 1), False), ((8, 16, 32), (1,), True),
+             ((7, 0), (1,), False)]
+
+
+@pytest.mark.parametrize("op", ["sum", "mean"])
+@pytest.mark.parametrize("trans", [False, True])
+def test_reductions(ex, op, trans):
+    g = torch.Generator().manual_seed(10)
+    s = ex.register_reduce(f"r|{op}", op)
+    pend = []
+    for shape, axes, keep in RED_CASES:
+        for dt in (torch.float32, torch.bfloat16):
+            if trans and len(shape) == 2:
+                x = torch.randn(shape[::-1], generator=g).to(dt).t()
+            else:
+                x = torch.randn(shape, generator=g).to(dt)
+            out_shape = list(x.shape)
+            for a in sorted(a % x.dim() for a in axes):
+                out_shape[a] = 1
+            if not keep:
+                out_shape = [d for i, d in enumerate(out_shape) if i not in [a % x.dim() for a in axes]]
+            go = torch.empty(out_shape, dtype=dt, device=DEV)
+            ex.reduce(s, gpu(x), go, axes, keep)
+            pend.append((x, go, axes, keep))
+    ex.flush(sync=True)
+    for x, go, axes, keep in pend:
+        check_reduce(op, x, go.cpu(), axes, keep)
+
+
+def test_reduce_stream(ext):
+    st = W.lastdim_reduce(n_req=96, seed=2, max_elems=1 << 20)
+    host_out = run_stream(ext, st)
+    for r in st.requests:
+        check_reduce(r.op, r.a.view(st.host_in), r.out.view(host_out).clone(), list(r.axes),
+                     r.keepdim)
+
+
+# --------------------------------------------------------------------------
+# hazards inside one flush, errors, lifecycle
+# --------------------------------------------------------------------------
+def test_dependent_chain_in_one_flush(ex):
+    """x = a + b; y = x * c; z = relu(y); a = a - z: read-after-write and
+    write-after-read inside a single batch run in submission order."""
+    g = torch.Generator().manual_seed(11)
+    n = 50000
+    a, b, c = (torch.randn(n, generator=g) for _ in range(3))
+    ga, gb, gc = gpu(a), gpu(b), gpu(c)
+    gx, gy, gz = (torch.empty(n, device=DEV) for _ in range(3))
+    relu = slot_of(ex, "relu")
+    ex.builtin(C.OP_ADD, ga, gb, gx)
+    ex.builtin(C.OP_MUL, gx, gc, gy)
+    ex.unary(relu, gy, gz)
+    ex.builtin(C.OP_SUB, ga, gz, ga)
+    ex.flush(sync=True)
+    x = a + b
+    y = x * c
+    z = torch.relu(y)
+    assert torch.equal(gz.cpu(), z)
+    assert torch.equal(ga.cpu(), a - z)
+
+
+def test_chain_across_async_flushes():
+    """Consecutive async flushes with a dependency are ordered too."""
+    with C.Executor(0, mode=C.MODE_PERSISTENT) as e:
+        n = 1 << 18
+        x = torch.zeros(n, device=DEV)
+        one = torch.ones(n, device=DEV)
+        for _ in range(50):
+            e.builtin(C.OP_ADD, x, one, x)
+            e.flush(sync=False)
+        e.flush(sync=True)
+        assert bool((x == 50).all())
+
+
+def test_unregistered_slot_reports_error(ex):
+    x = torch.randn(1000, device=DEV)
+    y = torch.empty_like(x)
+    ex.unary(77, x, y)
+    with pytest.raises(C.GpuosError, match="no registered operator"):
+        ex.flush(sync=True)
+    ex.builtin(C.OP_ADD, x, x, y)           # the executor stays usable
+    ex.flush(sync=True)
+    assert torch.equal(y, x + x)
+
+
+def test_bad_requests_rejected_on_host(ex):
+    a = torch.randn(4, 5, device=DEV)
+    with pytest.raises(C.GpuosError, match="broadcast"):
+        ex.builtin(C.OP_ADD, a, torch.randn(3, device=DEV), torch.empty(4, 5, device=DEV))
+    with pytest.raises(C.GpuosError):
+        ex.builtin(7, a, a, a)
+
+
+def test_persistent_lifecycle():
+    with C.Executor(0, mode=C.MODE_PERSISTENT, idle_ms=30) as e:
+        assert e.worker_alive()
+        x = torch.randn(10000, device=DEV)
+        y = torch.empty_like(x)
+        time.sleep(0.3)                       # idle exit after 30 ms
+        assert not e.worker_alive()
+        e.builtin(C.OP_MUL, x, x, y)
+        e.flush(sync=True)                    # relaunched on demand
+        assert torch.equal(y, x * x)
+        e.set_yield_every(1)                  # exit after every batch
+        for _ in range(5):
+            e.builtin(C.OP_ADD, x, y, y)
+            e.flush(sync=True)
+        st = e.stats()
+        assert st["relaunches"] >= 5, st
+        assert st["errors"] == 0
+        assert torch.allclose(y, x * x + 5 * x)
+
+
+def test_ext_api_surface(ext):
+    names = ["init", "shutdown", "abi_version", "set_debug_level", "set_verbose_level",
+             "peek_queue", "set_yield_every", "worker_alive", "submit_add", "submit_mul",
+             "submit_sub", "submit_div", "flush", "register_elementwise", "submit_unary",
+             "submit_binary", "register_reduce", "submit_reduce"]
+    for n in names:
+        assert hasattr(ext, n), n
+    assert ext.abi_version() == 1
+    q = ext.peek_queue()
+    for k in ("head", "tail", "in_flight", "capacity", "processed", "heartbeat", "quit",
+              "host_tail_shadow", "host_pending", "staging", "shard_size"):
+        assert k in q, k
+    a = torch.arange(16, device=DEV, dtype=torch.float32)
+    b = 2 * torch.ones_like(a)
+    c = torch.empty_like(a)
+    ext.submit_add(a, b, c)
+    ext.submit_mul(a, b, c)
+    ext.submit_sub(a, b, c)
+    ext.submit_div(a, b, c)
+    ext.flush(sync=True)
+    assert torch.equal(c, a / 2)            # the four ran in submission order
+    with pytest.raises(RuntimeError):
+        ext.submit_add(a.cpu(), b.cpu(), c.cpu())
+    with pytest.raises(TypeError):
+        ext.submit_add(a.long(), b, c)
+
+
+def test_stream_mode_orders_with_torch():
+    g = gpuos_b200.load()
+    g.init(4096, 256, mode="stream")
+    try:
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            a = torch.randn(1 << 20, device=DEV)
+            b = a * 3                      # produced on s
+            c = torch.empty_like(a)
+            g.submit_add(a, b, c)
+            g.flush(sync=False)            # runs on s after the producer
+            d = c * 2                      # consumer on s, no host sync
+        s.synchronize()
+        assert torch.equal(d, (a + a * 3) * 2)
+    finally:
+        g.shutdown()
