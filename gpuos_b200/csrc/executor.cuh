@@ -1,13 +1,19 @@
-// Batch executor: warps claim fixed-size chunks of a batch with one atomic
-// each and run the chunk through a layout-specific processor.
+// Batch executor building blocks: request records, jump-table resolution,
+// and the per-warp chunk processors (strided elementwise, reductions).  The
+// CTA pipeline that feeds them, and the staged vector path, are in
+// pipeline.cuh.
 //
 // Replaces the reference's op_batch (src/persistent_kernel.cu:81-112), which
 // walks the sub-tasks of a 512-task shard one after another inside a single
 // CTA with int64 div/mod index math per element, and the NVRTC operators of
 // pytorch_ext/gpuos_ext.cpp:625-679 (elementwise) and 726-806 (reduce), which
-// run one request per CTA.  Here every request is split into chunks and all
-// chunks of a batch are spread over every SM; contiguous and row-broadcast
-// requests move 16 bytes per lane per access.
+// run one request per CTA.  Here every request is split into chunks and the
+// chunks of a batch are spread over every SM.
+//
+// Chunks that are not staged through shared memory (misaligned views,
+// arbitrary strides up to 8 dims, reductions) run here, one warp per chunk.
+// A request record is decoded from eight 16-byte loads straight into
+// registers.
 //
 // Compiled by nvcc into the library and by NVRTC for custom expressions.
 #pragma once
@@ -20,6 +26,9 @@ namespace gpuos {
 
 #ifndef GPUOS_JIT_KNOWN
 #define GPUOS_JIT_KNOWN(v) false
+#endif
+#ifndef GPUOS_JIT_UNIT_CASES
+#define GPUOS_JIT_UNIT_CASES
 #endif
 
 __device__ __forceinline__ bool ew_known(int v) {
@@ -64,7 +73,57 @@ __device__ __forceinline__ uint32_t fdiv_u32(uint32_t n, uint32_t m, uint32_t s)
   return (__umulhi(n, m) + n) >> s;
 }
 
-__device__ __forceinline__ int64_t row_of(const Req& q, int64_t e) {
+// A request record in registers (fields as in struct Req).
+struct ReqView {
+  uint64_t a, b, o;
+  int64_t numel, inner, sa_row, sb_row, so_row, sa_in, sb_in;
+  uint32_t chunk, nseg, ext, part, cnt, fdiv_m, fdiv_s, rg;
+  int op, kind, layout, dta, dtb, dto, flags;
+  float p0, p1;
+};
+
+__device__ __forceinline__ uint64_t u64of(uint32_t lo, uint32_t hi) {
+  return ((uint64_t)hi << 32) | lo;
+}
+
+// Decode the 128-byte record from eight uniform 16-byte loads (L2, so that a
+// record restaged by the persistent worker is never read stale from L1).
+__device__ __forceinline__ ReqView load_req(const Req* g) {
+  const uint4* s = reinterpret_cast<const uint4*>(g);
+  const uint4 w0 = __ldcg(s + 0), w1 = __ldcg(s + 1), w2 = __ldcg(s + 2), w3 = __ldcg(s + 3);
+  const uint4 w4 = __ldcg(s + 4), w5 = __ldcg(s + 5), w6 = __ldcg(s + 6), w7 = __ldcg(s + 7);
+  ReqView q;
+  q.op = (int)(w0.x & 0xffffu);
+  q.kind = (int)((w0.x >> 16) & 0xffu);
+  q.layout = (int)(w0.x >> 24);
+  q.dta = (int)(w0.y & 0xffu);
+  q.dtb = (int)((w0.y >> 8) & 0xffu);
+  q.dto = (int)((w0.y >> 16) & 0xffu);
+  q.flags = (int)(w0.y >> 24);
+  q.p0 = __uint_as_float(w0.z);
+  q.p1 = __uint_as_float(w0.w);
+  q.chunk = w1.x;
+  q.nseg = w1.y;
+  q.numel = (int64_t)u64of(w1.z, w1.w);
+  q.a = u64of(w2.x, w2.y);
+  q.b = u64of(w2.z, w2.w);
+  q.o = u64of(w3.x, w3.y);
+  q.inner = (int64_t)u64of(w3.z, w3.w);
+  q.sa_row = (int64_t)u64of(w4.x, w4.y);
+  q.sb_row = (int64_t)u64of(w4.z, w4.w);
+  q.so_row = (int64_t)u64of(w5.x, w5.y);
+  q.sa_in = (int64_t)u64of(w5.z, w5.w);
+  q.sb_in = (int64_t)u64of(w6.x, w6.y);
+  q.ext = w6.z;
+  q.part = w6.w;
+  q.cnt = w7.x;
+  q.fdiv_m = w7.y;
+  q.fdiv_s = w7.z;
+  q.rg = w7.w;
+  return q;
+}
+
+__device__ __forceinline__ int64_t row_of(const ReqView& q, int64_t e) {
   if (q.flags & RF_BIG) return e / q.inner;
   return (int64_t)fdiv_u32((uint32_t)e, q.fdiv_m, q.fdiv_s);
 }
@@ -82,6 +141,8 @@ struct Exec {
   volatile uint64_t* done_ring; // completion words in mapped host memory (may be null)
   uint64_t* done_dev;           // device copy of the completion words (worker only)
   uint64_t wait_limit_ns;
+  uint64_t seq;                 // batch sequence number
+  uint32_t nchunk;              // chunks in the batch
   int lane;
 };
 
@@ -92,214 +153,56 @@ __device__ __forceinline__ void set_err(const Exec& ex, uint32_t bits) {
 // Jump-table resolution (alias -> physical slot -> variant + parameters).
 // The tables are read with plain volatile loads: the worker acquires at the
 // batch boundary, a launched kernel starts after the host's table writes.
-__device__ __forceinline__ int resolve(const Req& q, const Tables* tab, float& p0, float& p1) {
+__device__ __forceinline__ int resolve(const ReqView& q, const Tables* tab, float& p0, float& p1) {
   p0 = q.p0;
   p1 = q.p1;
   if (!(q.flags & RF_SLOT)) return q.op;
-  int s = q.op;
+  const int s = q.op;
   if (s < 0 || s >= kMaxSlots) return V_NONE;
   const volatile int32_t* al = tab->alias;
-  int phys = al[s];
+  const int phys = al[s];
   if (phys < 0 || phys >= kMaxSlots) return V_NONE;
   const volatile SlotEntry* se = &tab->slot[phys];
-  int v = se->variant;
+  const int v = se->variant;
   p0 = se->p0;
   p1 = se->p1;
   return v;
 }
 
 // ---------------------------------------------------------------------------
-// Elementwise, every operand contiguous over numel (or a broadcast scalar).
+// Elementwise generic path (one shared body): misaligned views, arbitrary
+// inner strides, and general strided requests of up to 8 dims.
 // ---------------------------------------------------------------------------
-__device__ __noinline__ void ew_contig(const Req& q, int v, float p0, float p1,
-                                       int64_t e0, int64_t e1, int lane) {
+__device__ __forceinline__ void ew_generic(const ReqView& q, const ExtRec* x, int v, float p0,
+                                           float p1, int64_t e0, int64_t e1, int lane) {
   const bool hasb = q.flags & RF_HAS_B;
-  const bool asc = q.flags & RF_A_SCALAR;
-  const bool bsc = q.flags & RF_B_SCALAR;
-  const float As = asc ? ld1(q.a, q.dta, 0) : 0.f;
-  const float Bs = (hasb && bsc) ? ld1(q.b, q.dtb, 0) : 0.f;
-  if (q.flags & RF_VEC) {
-    const int64_t eend = e1 & ~(int64_t)7;
-    int64_t e = e0 + 8 * lane;
-    for (; e + 256 < eend; e += 512) {
-      float A0[8], A1[8], B0[8], B1[8], R0[8], R1[8];
-      if (asc) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) { A0[k] = As; A1[k] = As; }
-      } else {
-        ld8(q.a, q.dta, e, A0);
-        ld8(q.a, q.dta, e + 256, A1);
-      }
-      if (hasb && !bsc) {
-        ld8(q.b, q.dtb, e, B0);
-        ld8(q.b, q.dtb, e + 256, B1);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) { B0[k] = Bs; B1[k] = Bs; }
-      }
-      ew_apply8(v, A0, B0, R0, p0, p1);
-      ew_apply8(v, A1, B1, R1, p0, p1);
-      st8(q.o, q.dto, e, R0);
-      st8(q.o, q.dto, e + 256, R1);
-    }
-    if (e < eend) {
-      float A0[8], B0[8], R0[8];
-      if (asc) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) A0[k] = As;
-      } else {
-        ld8(q.a, q.dta, e, A0);
-      }
-      if (hasb && !bsc) {
-        ld8(q.b, q.dtb, e, B0);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) B0[k] = Bs;
-      }
-      ew_apply8(v, A0, B0, R0, p0, p1);
-      st8(q.o, q.dto, e, R0);
-    }
-    const int64_t t = eend + lane;
-    if (t < e1) {
-      float A = asc ? As : ld1(q.a, q.dta, t);
-      float B = (hasb && !bsc) ? ld1(q.b, q.dtb, t) : Bs;
-      float r = 0.f;
-      ew_apply1(v, A, B, r, p0, p1);
-      st1(q.o, q.dto, t, r);
-    }
-    return;
-  }
-  // scalar path: 4 elements per lane per iteration, loads issued first
-  int64_t e = e0 + lane;
-  for (; e + 96 < e1; e += 128) {
-    float A[4], B[4], R[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      A[k] = asc ? As : ld1(q.a, q.dta, e + 32 * k);
-      B[k] = (hasb && !bsc) ? ld1(q.b, q.dtb, e + 32 * k) : Bs;
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) ew_apply1(v, A[k], B[k], R[k], p0, p1);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) st1(q.o, q.dto, e + 32 * k, R[k]);
-  }
-  for (; e < e1; e += 32) {
-    float A = asc ? As : ld1(q.a, q.dta, e);
-    float B = (hasb && !bsc) ? ld1(q.b, q.dtb, e) : Bs;
-    float r = 0.f;
-    ew_apply1(v, A, B, r, p0, p1);
-    st1(q.o, q.dto, e, r);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Elementwise over [rows, inner]: out(r, c) = o[r*so_row + c]; each input
-// x(r, c) = x[r*sx_row + c*sx_in].  Covers [B,N] op [N], [B,N] op [B,1],
-// transposed 2-D views and every request that collapses to two dims.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void ld8_or_splat(uint64_t p, int dt, int64_t row_off, int64_t col,
-                                             int64_t s_in, bool scalar, float sc, float* v) {
-  if (scalar) {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = sc;
-  } else if (s_in == 0) {
-    float x = ld1(p, dt, row_off);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = x;
-  } else {
-    ld8(p, dt, row_off + col, v);
-  }
-}
-
-__device__ __noinline__ void ew_row2d(const Req& q, int v, float p0, float p1,
-                                      int64_t e0, int64_t e1, int lane) {
-  const bool hasb = q.flags & RF_HAS_B;
-  const bool asc = q.flags & RF_A_SCALAR;
-  const bool bsc = q.flags & RF_B_SCALAR;
-  const float As = asc ? ld1(q.a, q.dta, 0) : 0.f;
-  const float Bs = (hasb && bsc) ? ld1(q.b, q.dtb, 0) : 0.f;
+  const int lay = q.layout;
   const int64_t N = q.inner;
-  if (q.flags & RF_VEC) {  // N % 8 == 0, so an 8-group never straddles rows
-    int64_t e = e0 + 8 * lane;
-    for (; e + 256 < e1; e += 512) {
-      const int64_t r0 = row_of(q, e), c0 = e - r0 * N;
-      const int64_t r1 = row_of(q, e + 256), c1 = e + 256 - r1 * N;
-      float A0[8], A1[8], B0[8], B1[8], R0[8], R1[8];
-      ld8_or_splat(q.a, q.dta, r0 * q.sa_row, c0, q.sa_in, asc, As, A0);
-      ld8_or_splat(q.a, q.dta, r1 * q.sa_row, c1, q.sa_in, asc, As, A1);
-      if (hasb) {
-        ld8_or_splat(q.b, q.dtb, r0 * q.sb_row, c0, q.sb_in, bsc, Bs, B0);
-        ld8_or_splat(q.b, q.dtb, r1 * q.sb_row, c1, q.sb_in, bsc, Bs, B1);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) { B0[k] = 0.f; B1[k] = 0.f; }
-      }
-      ew_apply8(v, A0, B0, R0, p0, p1);
-      ew_apply8(v, A1, B1, R1, p0, p1);
-      st8(q.o, q.dto, r0 * q.so_row + c0, R0);
-      st8(q.o, q.dto, r1 * q.so_row + c1, R1);
-    }
-    if (e < e1) {
-      const int64_t r0 = row_of(q, e), c0 = e - r0 * N;
-      float A0[8], B0[8], R0[8];
-      ld8_or_splat(q.a, q.dta, r0 * q.sa_row, c0, q.sa_in, asc, As, A0);
-      if (hasb) {
-        ld8_or_splat(q.b, q.dtb, r0 * q.sb_row, c0, q.sb_in, bsc, Bs, B0);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) B0[k] = 0.f;
-      }
-      ew_apply8(v, A0, B0, R0, p0, p1);
-      st8(q.o, q.dto, r0 * q.so_row + c0, R0);
-    }
-    return;
-  }
-  int64_t e = e0 + lane;
-  for (; e + 96 < e1; e += 128) {
-    float A[4], B[4], R[4];
-    int64_t oo[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int64_t ek = e + 32 * k;
-      const int64_t r = row_of(q, ek), c = ek - r * N;
-      A[k] = asc ? As : ld1(q.a, q.dta, r * q.sa_row + c * q.sa_in);
-      B[k] = hasb ? (bsc ? Bs : ld1(q.b, q.dtb, r * q.sb_row + c * q.sb_in)) : 0.f;
-      oo[k] = r * q.so_row + c;
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) ew_apply1(v, A[k], B[k], R[k], p0, p1);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) st1(q.o, q.dto, oo[k], R[k]);
-  }
-  for (; e < e1; e += 32) {
-    const int64_t r = row_of(q, e), c = e - r * N;
-    float A = asc ? As : ld1(q.a, q.dta, r * q.sa_row + c * q.sa_in);
-    float B = hasb ? (bsc ? Bs : ld1(q.b, q.dtb, r * q.sb_row + c * q.sb_in)) : 0.f;
-    float R = 0.f;
-    ew_apply1(v, A, B, R, p0, p1);
-    st1(q.o, q.dto, r * q.so_row + c, R);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Elementwise, general strides over up to 8 dims (extension record).
-// ---------------------------------------------------------------------------
-__device__ __noinline__ void ew_strided(const Req& q, const ExtRec* x, int v, float p0, float p1,
-                                        int64_t e0, int64_t e1, int lane) {
-  const bool hasb = q.flags & RF_HAS_B;
-  const int nd = x->ndim;
   for (int64_t e = e0 + lane; e < e1; e += 32) {
-    int64_t rem = e, oa = 0, ob = 0, oo = 0;
-    for (int d = nd - 1; d >= 0; --d) {
-      const int64_t sz = x->sizes[d];
-      const int64_t i = rem % sz;
-      rem /= sz;
-      oa += i * x->sa[d];
-      ob += i * x->sb[d];
-      oo += i * x->so[d];
+    int64_t oa, ob, oo;
+    if (lay == EL_CONTIG) {
+      oa = (q.flags & RF_A_SCALAR) ? 0 : e;
+      ob = (q.flags & RF_B_SCALAR) ? 0 : e;
+      oo = e;
+    } else if (lay == EL_ROW2D) {
+      const int64_t r = row_of(q, e), c = e - r * N;
+      oa = r * q.sa_row + c * q.sa_in;
+      ob = r * q.sb_row + c * q.sb_in;
+      oo = r * q.so_row + c;
+    } else {
+      int64_t rem = e;
+      oa = ob = oo = 0;
+      for (int d = __ldcg(&x->ndim) - 1; d >= 0; --d) {
+        const int64_t sz = __ldcg(&x->sizes[d]);
+        const int64_t i = rem % sz;
+        rem /= sz;
+        oa += i * __ldcg(&x->sa[d]);
+        ob += i * __ldcg(&x->sb[d]);
+        oo += i * __ldcg(&x->so[d]);
+      }
     }
-    float A = ld1(q.a, q.dta, oa);
-    float B = hasb ? ld1(q.b, q.dtb, ob) : 0.f;
+    const float A = ld1(q.a, q.dta, oa);
+    const float B = hasb ? ld1(q.b, q.dtb, ob) : 0.f;
     float R = 0.f;
     ew_apply1(v, A, B, R, p0, p1);
     st1(q.o, q.dto, oo, R);
@@ -328,7 +231,7 @@ __device__ __forceinline__ bool combine_arrive(const Exec& ex, uint32_t* cnt, ui
 
 // Rows contiguous: a lane group of q.rg lanes sums one row (nseg == 1), or the
 // whole warp sums one segment of a long row (nseg > 1).
-__device__ __noinline__ void red_rows(const Exec& ex, const Req& q, bool mean, uint32_t k) {
+__device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool mean, uint32_t k) {
   const int lane = ex.lane;
   const int64_t C = q.inner;
   const bool vec = q.flags & RF_VEC;
@@ -424,7 +327,7 @@ __device__ __noinline__ void red_rows(const Exec& ex, const Req& q, bool mean, u
 
 // Rows adjacent in memory (a transposed view): lanes own rows, so every step
 // of the column loop reads rg adjacent rows of cl columns.
-__device__ __noinline__ void red_cols(const Exec& ex, const Req& q, bool mean, uint32_t k) {
+__device__ __forceinline__ void red_cols(const Exec& ex, const ReqView& q, bool mean, uint32_t k) {
   const int lane = ex.lane;
   const int64_t C = q.inner, R = q.numel;
   const int rg = (int)q.rg, cl = 32 / rg;
@@ -473,27 +376,27 @@ __device__ __noinline__ void red_cols(const Exec& ex, const Req& q, bool mean, u
 // Anything else: one lane per output element, serial over the reduced
 // elements with the first reduced axis varying fastest (the order of the
 // reference's generic path, pytorch_ext/gpuos_ext.cpp:794-798).
-__device__ __noinline__ void red_generic(const Exec& ex, const Req& q, const ExtRec* x, bool mean,
-                                         uint32_t k) {
+__device__ __forceinline__ void red_generic(const Exec& ex, const ReqView& q, const ExtRec* x,
+                                            bool mean, uint32_t k) {
   const int64_t o0 = (int64_t)k * q.chunk;
   int64_t o1 = o0 + q.chunk;
   if (o1 > q.numel) o1 = q.numel;
-  const int nd = x->ndim, rd = x->rdim;
+  const int nd = __ldcg(&x->ndim), rd = __ldcg(&x->rdim);
   for (int64_t oi = o0 + ex.lane; oi < o1; oi += 32) {
     int64_t rem = oi, ib = 0, ob = 0;
     for (int d = nd - 1; d >= 0; --d) {
-      const int64_t sz = x->sizes[d];
+      const int64_t sz = __ldcg(&x->sizes[d]);
       const int64_t i = rem % sz;
       rem /= sz;
-      ib += i * x->sa[d];
-      ob += i * x->so[d];
+      ib += i * __ldcg(&x->sa[d]);
+      ob += i * __ldcg(&x->so[d]);
     }
     float acc = 0.f;
     for (int64_t rv = 0; rv < q.inner; ++rv) {
       int64_t t = rv, off = 0;
       for (int j = 0; j < rd; ++j) {
-        const int64_t sz = x->rsizes[j];
-        off += (t % sz) * x->rstrides[j];
+        const int64_t sz = __ldcg(&x->rsizes[j]);
+        off += (t % sz) * __ldcg(&x->rstrides[j]);
         t /= sz;
       }
       acc += ld1(q.a, q.dta, ib + off);
@@ -505,7 +408,7 @@ __device__ __noinline__ void red_generic(const Exec& ex, const Req& q, const Ext
 // ---------------------------------------------------------------------------
 // One chunk of one request.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void process_chunk(const Exec& ex, const Req& q, uint32_t k) {
+__device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, uint32_t k) {
   float p0, p1;
   const int v = resolve(q, ex.tab, p0, p1);
   if (q.kind == RK_EW) {
@@ -516,9 +419,7 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const Req& q, uint
     const int64_t e0 = (int64_t)k * q.chunk;
     int64_t e1 = e0 + q.chunk;
     if (e1 > q.numel) e1 = q.numel;
-    if (q.layout == EL_CONTIG) ew_contig(q, v, p0, p1, e0, e1, ex.lane);
-    else if (q.layout == EL_ROW2D) ew_row2d(q, v, p0, p1, e0, e1, ex.lane);
-    else ew_strided(q, reinterpret_cast<const ExtRec*>(ex.base + q.ext), v, p0, p1, e0, e1, ex.lane);
+    ew_generic(q, reinterpret_cast<const ExtRec*>(ex.base + q.ext), v, p0, p1, e0, e1, ex.lane);
     return;
   }
   if (v != V_SUM && v != V_MEAN) {
@@ -529,23 +430,6 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const Req& q, uint
   if (q.layout == RL_ROWS) red_rows(ex, q, mean, k);
   else if (q.layout == RL_COLS) red_cols(ex, q, mean, k);
   else red_generic(ex, q, reinterpret_cast<const ExtRec*>(ex.base + q.ext), mean, k);
-}
-
-__device__ __forceinline__ void load_req(const Req* src, Req& dst) {
-  const uint4* s = reinterpret_cast<const uint4*>(src);
-  uint4* d = reinterpret_cast<uint4*>(&dst);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) d[i] = __ldcg(s + i);
-}
-
-// index of the request that owns chunk c: s_cb[r] <= c < s_cb[r + 1]
-__device__ __forceinline__ int find_req(const uint32_t* s_cb, int nreq, uint32_t c) {
-  int lo = 0, hi = nreq - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (s_cb[mid] <= c) lo = mid; else hi = mid - 1;
-  }
-  return lo;
 }
 
 // Lane 0 waits (bounded) until `target` chunks of the batch are done.
@@ -567,13 +451,13 @@ __device__ __forceinline__ bool wait_chunks_done(const Exec& ex, uint32_t target
 }
 
 // Called by the warp that finished the last chunk of the batch.  The
-// completion word is seq + 1 with the batch's error bits in the top byte.
+// completion word is seq + 1 with the batch's error bits in bits 48..55.
 __device__ __forceinline__ void finish_batch(const Exec& ex) {
   __threadfence();
   ex.st->t_last = globaltimer();
-  const uint64_t seq = ex.h->seq;
+  const uint64_t seq = ex.seq;
   const uint32_t err = atomicOr(&ex.st->err, 0u);
-  const uint64_t word = (seq + 1) | ((uint64_t)(err & 0xffu) << 56);
+  const uint64_t word = (seq + 1) | ((uint64_t)(err & 0xffu) << 48);
   if (ex.done_dev) st_release_gpu_u64(&ex.done_dev[seq % kDoneRing], word);
   if (ex.done_ring) {
     __threadfence_system();
@@ -581,108 +465,33 @@ __device__ __forceinline__ void finish_batch(const Exec& ex) {
   }
 }
 
-// Count `n` finished chunks.  Every lane releases its stores first, so a warp
-// that sees the count (a stage waiter, the finisher) also sees the data.
-__device__ __forceinline__ void arrive_done(const Exec& ex, uint32_t n) {
-  __threadfence();
-  __syncwarp();
-  if (ex.lane == 0 && n != 0u) {
-    const uint32_t d = atomicAdd(&ex.st->done, n) + n;
-    if (d == ex.h->nchunk) finish_batch(ex);
-  }
-}
-
-// The claim loop of one warp over one batch.  s_cb is the CTA's shared copy of
-// the chunk prefix array.  Without stage barriers a warp reports its finished
-// chunks once, when it runs out of work; with them it reports every chunk, so
-// that warps waiting on an earlier stage are never waiting on it.
-__device__ void run_batch_warp(const Exec& ex, const uint32_t* s_cb) {
-  const uint32_t nchunk = ex.h->nchunk;
-  const int nreq = (int)ex.h->nreq;
-  const int lane = ex.lane;
-  const bool staged = ex.req_wait != nullptr;
-  uint32_t c = 0;
-  if (lane == 0) {
-    c = atomicAdd(&ex.st->claim, 1u);
-    if (c == 0) ex.st->t_first = globaltimer();
-  }
-  c = __shfl_sync(GPUOS_FULL, c, 0);
-  int r = -1;
-  uint32_t rbase = 0, rend = 0, mine = 0;
-  Req q;
-  while (c < nchunk) {
-    uint32_t cn = 0;
-    if (lane == 0) cn = atomicAdd(&ex.st->claim, 1u);
-    if (r < 0 || c >= rend || c < rbase) {
-      r = find_req(s_cb, nreq, c);
-      rbase = s_cb[r];
-      rend = s_cb[r + 1];
-      load_req(ex.recs + r, q);
-    }
-    bool run = true;
-    if (staged) {
-      const uint32_t w = __ldcg(ex.req_wait + r);
-      if (w != 0u && !wait_chunks_done(ex, w)) {
-        if (lane == 0) set_err(ex, ERR_STAGE_TIMEOUT);
-        run = false;
-      }
-    }
-    if (run) process_chunk(ex, q, c - rbase);
-    if (staged) arrive_done(ex, 1u);
-    else ++mine;
-    c = __shfl_sync(GPUOS_FULL, cn, 0);
-  }
-  if (!staged) arrive_done(ex, mine);
-}
-
 // Bind the execution context of one batch payload.
 __device__ __forceinline__ Exec bind_batch(const uint8_t* payload, const Tables* tab,
                                            volatile uint64_t* done_ring, uint64_t* done_dev,
                                            uint64_t wait_limit_ns) {
+  // the header is read through L2: the persistent worker reuses payload memory
   const BatchHdr* h = reinterpret_cast<const BatchHdr*>(payload);
   Exec ex;
   ex.base = payload;
   ex.h = h;
   ex.st = reinterpret_cast<BatchState*>(const_cast<uint8_t*>(payload) + sizeof(BatchHdr));
-  ex.recs = reinterpret_cast<const Req*>(payload + h->rec_off);
-  ex.req_wait = (h->flags & BF_STAGED)
-                    ? reinterpret_cast<const uint32_t*>(payload + h->cb_off) + (h->nreq + 1)
+  ex.recs = reinterpret_cast<const Req*>(payload + __ldcg(&h->rec_off));
+  const uint32_t flags = __ldcg(&h->flags);
+  const uint32_t gran = __ldcg(&h->gran), nch = __ldcg(&h->nchunk);
+  ex.req_wait = (flags & BF_STAGED)
+                    ? reinterpret_cast<const uint32_t*>(payload + __ldcg(&h->gtab_off)) +
+                          (nch + gran - 1) / gran
                     : nullptr;
   ex.tab = tab;
-  ex.scratch = reinterpret_cast<float*>(h->scratch);
-  ex.counters = reinterpret_cast<uint32_t*>(h->counters);
+  ex.scratch = reinterpret_cast<float*>(__ldcg(&h->scratch));
+  ex.counters = reinterpret_cast<uint32_t*>(__ldcg(&h->counters));
+  ex.seq = __ldcg(&h->seq);
+  ex.nchunk = __ldcg(&h->nchunk);
   ex.done_ring = done_ring;
   ex.done_dev = done_dev;
   ex.wait_limit_ns = wait_limit_ns;
   ex.lane = threadIdx.x & 31;
   return ex;
-}
-
-// CTA-level entry for one batch: copy the chunk prefix into shared memory,
-// run every warp's claim loop, then count this CTA out of the batch.  The CTA
-// that leaves last retires the batch: nobody reads its payload any more, so
-// the host may reuse the memory.
-__device__ __forceinline__ void run_batch_cta(const uint8_t* payload, const Tables* tab,
-                                              volatile uint64_t* done_ring, uint64_t* done_dev,
-                                              volatile uint64_t* retired_ring, uint32_t nctas,
-                                              uint64_t wait_limit_ns, uint32_t* s_cb) {
-  const BatchHdr* h = reinterpret_cast<const BatchHdr*>(payload);
-  const uint32_t nreq = h->nreq;
-  const uint32_t* cb = reinterpret_cast<const uint32_t*>(payload + h->cb_off);
-  for (uint32_t i = threadIdx.x; i <= nreq; i += blockDim.x) s_cb[i] = __ldcg(cb + i);
-  __syncthreads();
-  Exec ex = bind_batch(payload, tab, done_ring, done_dev, wait_limit_ns);
-  run_batch_warp(ex, s_cb);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t left = atomicAdd(&ex.st->ctas_left, 1u) + 1u;
-    if (left == nctas && retired_ring) {
-      __threadfence_system();
-      const uint64_t seq = h->seq;
-      st_release_sys_u64(&retired_ring[seq % kDoneRing], seq + 1);
-    }
-  }
 }
 
 }  // namespace gpuos

@@ -13,8 +13,10 @@
 #include <torch/csrc/autograd/python_variable.h>
 
 #include <cstring>
+#include <deque>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/gpuos_b200.h"
 
@@ -26,6 +28,40 @@ gpuos_options g_opt;
 bool g_have_opt = false;
 int g_verbose = 0;
 std::mutex g_mu;
+
+// Tensors of submitted requests stay referenced until the batch that reads
+// them is done, so that dropping the Python objects (or the caching allocator
+// handing their memory to a new tensor) cannot corrupt a pending request.
+// All of this runs with the GIL held.
+struct Keep {
+  uint64_t ticket;
+  std::vector<PyObject*> objs;
+};
+std::vector<PyObject*> g_pending_refs[kMaxDev];
+std::deque<Keep> g_inflight_refs[kMaxDev];
+
+inline void keep(int dev, PyObject* o) {
+  Py_INCREF(o);
+  g_pending_refs[dev].push_back(o);
+}
+
+void release_done(int dev, bool all) {
+  auto& q = g_inflight_refs[dev];
+  uint64_t done = UINT64_MAX;
+  if (!all) {
+    gpuos_stats st;
+    if (!g_ex[dev] || gpuos_get_stats(g_ex[dev], &st) != GPUOS_OK) return;
+    done = st.processed;
+  }
+  while (!q.empty() && q.front().ticket <= done) {
+    for (PyObject* o : q.front().objs) Py_DECREF(o);
+    q.pop_front();
+  }
+  if (all) {
+    for (PyObject* o : g_pending_refs[dev]) Py_DECREF(o);
+    g_pending_refs[dev].clear();
+  }
+}
 
 PyObject* raise_status(int32_t rc) {
   const char* msg = gpuos_last_error();
@@ -172,6 +208,7 @@ PyObject* py_shutdown(PyObject*, PyObject*) {
       first_rc = rc;
       err = gpuos_last_error();
     }
+    release_done(d, true);
   }
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -289,6 +326,9 @@ PyObject* submit_builtin(int op, PyObject* const* args, Py_ssize_t n) {
   if (!ex) return nullptr;
   const int32_t rc = gpuos_submit_builtin(ex, op, &a, &b, &o);
   if (rc != GPUOS_OK) return raise_status(rc);
+  keep(dout, args[0]);
+  keep(dout, args[1]);
+  keep(dout, args[2]);
   Py_RETURN_NONE;
 }
 
@@ -315,6 +355,8 @@ PyObject* py_submit_unary(PyObject*, PyObject* const* args, Py_ssize_t n) {
   if (!ex) return nullptr;
   const int32_t rc = gpuos_submit_unary(ex, (int32_t)slot, &a, &o);
   if (rc != GPUOS_OK) return raise_status(rc);
+  keep(dout, args[1]);
+  keep(dout, args[2]);
   Py_RETURN_NONE;
 }
 
@@ -338,6 +380,9 @@ PyObject* py_submit_binary(PyObject*, PyObject* const* args, Py_ssize_t n) {
   if (!ex) return nullptr;
   const int32_t rc = gpuos_submit_binary(ex, (int32_t)slot, &a, &b, &o);
   if (rc != GPUOS_OK) return raise_status(rc);
+  keep(dout, args[1]);
+  keep(dout, args[2]);
+  keep(dout, args[3]);
   Py_RETURN_NONE;
 }
 
@@ -369,12 +414,14 @@ PyObject* py_submit_reduce(PyObject*, PyObject* const* args, Py_ssize_t n) {
   }
   Py_DECREF(seq);
   if (PyErr_Occurred()) return nullptr;
-  const int keep = PyObject_IsTrue(args[4]);
-  if (keep < 0) return nullptr;
+  const int keepdim = PyObject_IsTrue(args[4]);
+  if (keepdim < 0) return nullptr;
   gpuos_executor* ex = executor_for(dout);
   if (!ex) return nullptr;
-  const int32_t rc = gpuos_submit_reduce(ex, (int32_t)slot, &x, &o, axes, (int32_t)na, keep);
+  const int32_t rc = gpuos_submit_reduce(ex, (int32_t)slot, &x, &o, axes, (int32_t)na, keepdim);
   if (rc != GPUOS_OK) return raise_status(rc);
+  keep(dout, args[1]);
+  keep(dout, args[2]);
   Py_RETURN_NONE;
 }
 
@@ -389,8 +436,14 @@ PyObject* py_flush(PyObject*, PyObject* args, PyObject* kw) {
     cudaStream_t s = nullptr;
     if (!current_stream(d, &s)) return nullptr;
     int32_t rc;
-    Py_BEGIN_ALLOW_THREADS rc = gpuos_flush(ex, sync, s, nullptr);
+    uint64_t ticket = 0;
+    Py_BEGIN_ALLOW_THREADS rc = gpuos_flush(ex, sync, s, &ticket);
     Py_END_ALLOW_THREADS if (rc != GPUOS_OK) return raise_status(rc);
+    if (!g_pending_refs[d].empty()) {
+      g_inflight_refs[d].push_back(Keep{ticket, std::move(g_pending_refs[d])});
+      g_pending_refs[d].clear();
+    }
+    release_done(d, false);
   }
   Py_RETURN_NONE;
 }

@@ -144,8 +144,9 @@ struct alignas(16) BatchHdr {
   uint64_t scratch;      // device address of this batch's partials area (floats)
   uint64_t counters;     // device address of the counter pool (u32, self-cleaning)
   uint64_t wait_from;    // BF_AFTER_PREV: batches [wait_from, seq) must be done first
-  uint32_t dev_off;      // byte offset of this payload in the device staging ring
-  uint32_t pad;
+  uint32_t gtab_off;     // byte offset of uint32 gtab[ceil(nchunk / gran)]: request of
+                         // the first chunk of every granule
+  uint32_t gran;         // chunks per granule (the unit a producer takes at a time)
 };
 static_assert(sizeof(BatchHdr) == 64, "BatchHdr must stay 64 bytes");
 

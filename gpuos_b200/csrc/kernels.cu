@@ -2,26 +2,35 @@
 //
 //  gpuos_batch_kernel   one launch per batch, stream-ordered with the caller's
 //                       CUDA stream (the mode that interoperates with torch
-//                       streams and CUDA graphs).
+//                       streams and CUDA graphs).  One pipeline CTA per SM
+//                       (pipeline.cuh).
 //  gpuos_worker_kernel  the persistent worker: CTA 0 polls the doorbell in
 //                       mapped host memory and stages published batches into
-//                       the device ring; every other CTA walks the batches in
-//                       order and claims chunks warp by warp.  Replaces
+//                       the device ring; every other CTA is a pipeline that
+//                       walks the batches in order, its producer warp moving
+//                       from one batch to the next without draining.  Replaces
 //                       persistent_worker (src/persistent_kernel.cu:133-200),
 //                       whose thread 0 CAS-claims one 496-byte Task per CTA.
 //
 // Every wait in these kernels is bounded by %globaltimer.
-#include "executor.cuh"
+#include "pipeline.cuh"
 
 namespace gpuos {
 
-static constexpr int kBlockMax = 1024;
-
-extern "C" __global__ void __launch_bounds__(kBlockMax)
+extern "C" __global__ void __launch_bounds__(kCtaThreads, 1)
 gpuos_batch_kernel(const uint8_t* payload, const Tables* tab, volatile uint64_t* done_ring,
                    volatile uint64_t* retired_ring, uint64_t wait_limit_ns) {
-  __shared__ uint32_t s_cb[kMaxReqPerBatch + 1];
-  run_batch_cta(payload, tab, done_ring, nullptr, retired_ring, gridDim.x, wait_limit_ns, s_cb);
+  extern __shared__ __align__(128) uint8_t smem[];
+  PipeSmem* sm = pipe_init(smem);
+  uint8_t* bufs = smem + pipe_buf_offset();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    Producer P{sm, bufs, 0, 0, wait_limit_ns, false};
+    produce_batch(P, payload, tab, nullptr, blockIdx.x, gridDim.x, lane);
+    produce_stop(P, lane);
+  } else {
+    consume(sm, bufs, tab, done_ring, nullptr, retired_ring, gridDim.x, wait_limit_ns);
+  }
 }
 
 // Copy `bytes` (multiple of 16, both ends 16-byte aligned) from mapped host
@@ -104,88 +113,99 @@ __device__ void ingest_loop(const WorkerArgs& w) {
   }
 }
 
-// CTAs 1..n: walk the staged batches in order.
-__device__ void process_loop(const WorkerArgs& w, uint32_t* s_cb) {
-  __shared__ int s_go;
-  __shared__ uint32_t s_off;
+// CTAs 1..n: a pipeline over the staged batches, in order.
+__device__ void pipeline_loop(const WorkerArgs& w, uint8_t* smem) {
+  PipeSmem* sm = pipe_init(smem);
+  uint8_t* bufs = smem + pipe_buf_offset();
   const uint32_t nproc = gridDim.x - 1;
-  // bound for waiting on the next batch: the ingest stops the worker after
-  // idle_ns without work, so waiting much longer than that means it is gone
-  const uint64_t limit = w.idle_ns + 2000000000ull;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the ingest stops the worker after idle_ns without work, so waiting much
+  // longer than that for the next batch means it is gone
+  const uint64_t idle_limit = w.idle_ns + 2000000000ull;
+  if (warp != 0) {
+    consume(sm, bufs, w.tab, w.done_ring, w.dctrl->done_dev, w.retired_ring, nproc,
+            idle_limit + w.wait_limit_ns);
+    return;
+  }
+  Producer P{sm, bufs, 0, 0, w.wait_limit_ns, false};
   for (uint64_t s = w.start_seq;; ++s) {
-    if (threadIdx.x == 0) {
-      int go = 0;
+    int go = 0;
+    uint32_t off = 0;
+    if (lane == 0) {
       const uint64_t t0 = globaltimer();
       unsigned backoff = 32;
-      while (true) {
+      while (!P.dead) {
         if (ld_acquire_u64(&w.dctrl->ready) > s) { go = 1; break; }
         if (ld_acquire_u64(&w.dctrl->stop_at) <= s) break;
-        if (globaltimer() - t0 > limit) {
+        if (globaltimer() - t0 > idle_limit) {
           w.hctrl->err = w.hctrl->err | ERR_IDLE_EXIT;
           break;
         }
         __nanosleep(backoff);
         if (backoff < 2048) backoff <<= 1;
       }
-      s_go = go;
-      if (go) s_off = *reinterpret_cast<volatile uint32_t*>(&w.dctrl->ready_off[s % kDoneRing]);
+      if (go) off = *reinterpret_cast<volatile uint32_t*>(&w.dctrl->ready_off[s % kDoneRing]);
     }
-    __syncthreads();
-    if (!s_go) return;
-    const uint8_t* payload = w.ring + s_off;
-    const BatchHdr* h = reinterpret_cast<const BatchHdr*>(payload);
-    if (h->flags & BF_AFTER_PREV) {
-      // a hazard with an earlier batch: wait (bounded) until every batch in
-      // [wait_from, s) has completed
-      if (threadIdx.x == 0) {
-        const uint64_t t0 = globaltimer();
-        for (uint64_t j = h->wait_from; j < s; ++j) {
-          while ((ld_acquire_u64(&w.dctrl->done_dev[j % kDoneRing]) & ((1ull << 56) - 1)) != j + 1) {
-            __nanosleep(256);
-            if (globaltimer() - t0 > w.wait_limit_ns) break;
-          }
-        }
-      }
-      __syncthreads();
-    }
-    run_batch_cta(payload, w.tab, w.done_ring, w.dctrl->done_dev, w.retired_ring, nproc,
-                  w.wait_limit_ns, s_cb);
-    __syncthreads();
+    go = __shfl_sync(GPUOS_FULL, go, 0);
+    off = __shfl_sync(GPUOS_FULL, off, 0);
+    if (!go) break;
+    produce_batch(P, w.ring + off, w.tab, w.dctrl->done_dev, blockIdx.x - 1, nproc, lane);
+    const int dead = __shfl_sync(GPUOS_FULL, P.dead ? 1 : 0, 0);
+    if (dead) break;
   }
+  produce_stop(P, lane);
 }
 
-extern "C" __global__ void __launch_bounds__(kBlockMax) gpuos_worker_kernel(WorkerArgs w) {
-  __shared__ uint32_t s_cb[kMaxReqPerBatch + 1];
+extern "C" __global__ void __launch_bounds__(kCtaThreads, 1) gpuos_worker_kernel(WorkerArgs w) {
+  extern __shared__ __align__(128) uint8_t smem[];
   if (blockIdx.x == 0) ingest_loop(w);
-  else process_loop(w, s_cb);
+  else pipeline_loop(w, smem);
 }
 
 }  // namespace gpuos
 
 // ---- launch wrappers used by the host runtime ------------------------------
+extern "C" size_t gpuos_pipe_smem_bytes() { return gpuos::pipe_smem_bytes(); }
+extern "C" int gpuos_cta_threads() { return gpuos::kCtaThreads; }
+extern "C" int gpuos_unit_elems() { return gpuos::kUnit; }
+
+// Opt in to the dynamic shared memory of a pipeline CTA (current device).
+extern "C" cudaError_t gpuos_kernel_setup() {
+  const int bytes = (int)gpuos::pipe_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(gpuos::gpuos_batch_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(gpuos::gpuos_worker_kernel,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
 extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::Tables* tab,
                                           volatile uint64_t* done_ring,
                                           volatile uint64_t* retired_ring, uint64_t wait_limit_ns,
                                           int grid, int block, cudaStream_t stream) {
-  gpuos::gpuos_batch_kernel<<<grid, block, 0, stream>>>(payload, tab, done_ring, retired_ring,
-                                                        wait_limit_ns);
+  (void)block;
+  gpuos::gpuos_batch_kernel<<<grid, gpuos::kCtaThreads, gpuos::pipe_smem_bytes(), stream>>>(
+      payload, tab, done_ring, retired_ring, wait_limit_ns);
   return cudaGetLastError();
 }
 
 extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, int block,
                                            cudaStream_t stream) {
+  (void)block;
   const gpuos::WorkerArgs* w = static_cast<const gpuos::WorkerArgs*>(args);
-  gpuos::gpuos_worker_kernel<<<grid, block, 0, stream>>>(*w);
+  gpuos::gpuos_worker_kernel<<<grid, gpuos::kCtaThreads, gpuos::pipe_smem_bytes(), stream>>>(*w);
   return cudaGetLastError();
 }
 
 extern "C" cudaError_t gpuos_occupancy(int block, int* batch_blocks_per_sm,
                                        int* worker_blocks_per_sm) {
+  (void)block;
+  const size_t smem = gpuos::pipe_smem_bytes();
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      batch_blocks_per_sm, gpuos::gpuos_batch_kernel, block, 0);
+      batch_blocks_per_sm, gpuos::gpuos_batch_kernel, gpuos::kCtaThreads, smem);
   if (e != cudaSuccess) return e;
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(worker_blocks_per_sm,
-                                                       gpuos::gpuos_worker_kernel, block, 0);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      worker_blocks_per_sm, gpuos::gpuos_worker_kernel, gpuos::kCtaThreads, smem);
 }
 
 extern "C" size_t gpuos_worker_args_size() { return sizeof(gpuos::WorkerArgs); }

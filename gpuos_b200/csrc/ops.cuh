@@ -49,21 +49,11 @@ __device__ __forceinline__ float op1(float A, float B, float p0, float p1) {
   else return A;  // V_COPY
 }
 
-template <int V>
-__device__ __forceinline__ void op8(const float* A, const float* B, float* R, float p0, float p1) {
-#pragma unroll
-  for (int k = 0; k < 8; ++k) R[k] = op1<V>(A[k], B[k], p0, p1);
-}
-
 // Custom (NVRTC) expressions are spliced in here by the JIT executor source.
-#ifndef GPUOS_JIT_CASES8
-#define GPUOS_JIT_CASES8
-#endif
 #ifndef GPUOS_JIT_CASES1
 #define GPUOS_JIT_CASES1
 #endif
 
-#define GPUOS_CASE8(V) case V: op8<V>(A, B, R, p0, p1); return true;
 #define GPUOS_CASE1(V) case V: r = op1<V>(A, B, p0, p1); return true;
 #define GPUOS_ALL_EW(M) \
   M(V_ADD) M(V_MUL) M(V_SUB) M(V_DIV0) M(V_DIV) M(V_MAX) M(V_MIN) M(V_POW) \
@@ -71,22 +61,33 @@ __device__ __forceinline__ void op8(const float* A, const float* B, float* R, fl
   M(V_HARDSIGMOID) M(V_HARDSWISH) M(V_GELU) M(V_SIN) M(V_COS) M(V_LEAKY_RELU) \
   M(V_CLAMP) M(V_ELU) M(V_SOFTPLUS) M(V_CLAMP_MIN) M(V_CLAMP_MAX) M(V_COPY)
 
-// Apply variant v to 8 lanes of values.  The switch is uniform per chunk.
-__device__ __forceinline__ bool ew_apply8(int v, const float* A, const float* B, float* R,
-                                          float p0, float p1) {
-  switch (v) {
-    GPUOS_ALL_EW(GPUOS_CASE8)
-    GPUOS_JIT_CASES8
-    default: return false;
-  }
-}
-
 __device__ __forceinline__ bool ew_apply1(int v, float A, float B, float& r, float p0, float p1) {
   switch (v) {
     GPUOS_ALL_EW(GPUOS_CASE1)
     GPUOS_JIT_CASES1
     default: return false;
   }
+}
+
+// Groups of 4 elements each lane handles per iteration of the vector loop
+// (the loop keeps the next iteration's loads in flight while it computes the
+// current one, so twice this many groups are live): 2 for the cheap,
+// memory-bound operators, 1 for those with a division, square root or
+// transcendental (compute heavy: a smaller body keeps the instruction cache
+// warm and the register budget low).
+template <int V>
+__device__ __forceinline__ constexpr int op_unroll() {
+  return (V == V_POW || V == V_SIGMOID || V == V_TANH || V == V_EXP || V == V_LOG ||
+          V == V_GELU || V == V_SIN || V == V_COS || V == V_ELU || V == V_SOFTPLUS ||
+          V == V_DIV || V == V_DIV0 || V == V_SQRT || V == V_HARDSWISH)
+             ? 1
+             : 2;
+}
+
+template <int V>
+__device__ __forceinline__ void op4(const float* A, const float* B, float* R, float p0, float p1) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) R[k] = op1<V>(A[k], B[k], p0, p1);
 }
 
 // ---- scalar load / store (element offsets) -------------------------------
@@ -127,6 +128,45 @@ __device__ __forceinline__ void ld8(uint64_t base, int dt, int64_t e, float* v) 
       bf2_to_f(u.x, v[0], v[1]); bf2_to_f(u.y, v[2], v[3]);
       bf2_to_f(u.z, v[4], v[5]); bf2_to_f(u.w, v[6], v[7]);
     }
+  }
+}
+
+// 4-element vector load / store: `e` is a multiple of 4 and the address is
+// aligned to 4 elements (16 bytes for fp32, 8 for fp16 / bf16).
+__device__ __forceinline__ void ld4(uint64_t base, int dt, int64_t e, float* v) {
+  if (dt == kF32) {
+    const float4 x = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e);
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(base) + e);
+    if (dt == kF16) {
+      float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+      v[0] = f.x; v[1] = f.y;
+      f = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+      v[2] = f.x; v[3] = f.y;
+    } else {
+      bf2_to_f(u.x, v[0], v[1]);
+      bf2_to_f(u.y, v[2], v[3]);
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t f2_to_h2(float a, float b);
+__device__ __forceinline__ uint32_t f2_to_bf2(float a, float b);
+
+__device__ __forceinline__ void st4(uint64_t base, int dt, int64_t e, const float* v) {
+  if (dt == kF32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + e) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+    uint2 u;
+    if (dt == kF16) {
+      u.x = f2_to_h2(v[0], v[1]);
+      u.y = f2_to_h2(v[2], v[3]);
+    } else {
+      u.x = f2_to_bf2(v[0], v[1]);
+      u.y = f2_to_bf2(v[2], v[3]);
+    }
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(base) + e) = u;
   }
 }
 

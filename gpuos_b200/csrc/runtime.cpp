@@ -27,6 +27,9 @@ extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, int block
                                            cudaStream_t stream);
 extern "C" cudaError_t gpuos_occupancy(int block, int* batch_blocks_per_sm,
                                        int* worker_blocks_per_sm);
+extern "C" cudaError_t gpuos_kernel_setup();
+extern "C" int gpuos_cta_threads();
+extern "C" int gpuos_unit_elems();
 
 namespace gpuos {
 
@@ -41,7 +44,7 @@ thread_local std::string t_last_error;
       throw GError(GPUOS_ECUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));  \
   } while (0)
 
-constexpr uint64_t kDoneMask = (1ull << 56) - 1;
+constexpr uint64_t kDoneMask = (1ull << 48) - 1;
 
 inline bool dt_ok(int dt) { return dt == kF32 || dt == kF16 || dt == kBF16; }
 inline int esz(int dt) { return dt == kF32 ? 4 : 2; }
@@ -171,6 +174,12 @@ bool RingAlloc::alloc(uint64_t size, uint64_t tag, uint64_t* off) {
 
 void RingAlloc::free_before(uint64_t upto) {
   while (!live_.empty() && live_.front().tag < upto) live_.pop_front();
+}
+
+// Transcendental operators: compute-heavy chunks, sized smaller.
+bool is_heavy(int v) {
+  return v == V_POW || v == V_SIGMOID || v == V_TANH || v == V_EXP || v == V_LOG ||
+         v == V_GELU || v == V_SIN || v == V_COS || v == V_ELU || v == V_SOFTPLUS;
 }
 
 // Operator names accepted by gpuos_variant_by_name (and the Python layer).
@@ -325,16 +334,20 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
 
   GCU(cudaFree(nullptr));
   GCU(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, device));
-  block_ = tpb;
+  GCU(gpuos_kernel_setup());
+  // The CTA shape is fixed by the kernels (one producer warp and eight
+  // consumer warps); threads_per_block is accepted for API compatibility.
+  block_ = gpuos_cta_threads();
   int bbps = 0, wbps = 0;
   GCU(gpuos_occupancy(block_, &bbps, &wbps));
-  if (bbps < 1 || wbps < 1) throw GError(GPUOS_ECUDA, "kernel cannot be resident with this block size");
+  if (bbps < 1 || wbps < 1) throw GError(GPUOS_ECUDA, "pipeline CTA cannot be resident");
   batch_bps_ = bbps;
-  // The worker keeps about 16 warps per SM: enough bytes in flight to stream
-  // HBM, while leaving room for other kernels next to the resident grid.
-  int wanted = opt_.blocks_per_sm > 0 ? opt_.blocks_per_sm : std::max(1, 512 / block_);
-  wanted = std::min(wanted, wbps);
-  grid_ = sm_count_ * wanted;
+  // one pipeline CTA per SM; the persistent worker adds its ingest CTA in
+  // place of one of them
+  grid_ = sm_count_;
+  const int pipelines = opt_.mode == GPUOS_MODE_PERSISTENT ? grid_ - 1 : sm_count_ * batch_bps_;
+  total_warps_ = pipelines * 8;
+  unit_elems_ = gpuos_unit_elems();
 
   GCU(cudaStreamCreateWithFlags(&s_worker_, cudaStreamNonBlocking));
   GCU(cudaStreamCreateWithFlags(&s_ctrl_, cudaStreamNonBlocking));
@@ -460,7 +473,7 @@ void build_ew(Pending& p, int op, bool is_slot, float p0, float p1,
     if (cd[i].a != 0) a_sc = false;
     if (cd[i].b != 0) b_sc = false;
   }
-  auto al16 = [](uint64_t x) { return (x & 15) == 0; };
+  auto al4 = [](uint64_t x, int e) { return (x % (uint64_t)(4 * e)) == 0; };
 
   if (m <= 1 && (m == 0 || cd[0].o == 1) &&
       (m == 0 || cd[0].a == 0 || cd[0].a == 1) &&
@@ -468,7 +481,8 @@ void build_ew(Pending& p, int op, bool is_slot, float p0, float p1,
     q.layout = EL_CONTIG;
     if (a_sc) q.flags |= RF_A_SCALAR;
     if (b_sc) q.flags |= RF_B_SCALAR;
-    bool vec = al16(q.o) && (a_sc || al16(q.a)) && (!b || b_sc || al16(q.b));
+    // vector path: every vector operand aligned to 4 of its elements
+    const bool vec = al4(q.o, eo) && (a_sc || al4(q.a, ea)) && (!b || b_sc || al4(q.b, eb));
     if (vec) q.flags |= RF_VEC;
   } else if (m <= 2 && cd[m - 1].o == 1) {
     const int64_t R = (m == 2) ? cd[0].n : 1, N = cd[m - 1].n;
@@ -481,14 +495,16 @@ void build_ew(Pending& p, int op, bool is_slot, float p0, float p1,
     q.sb_in = cd[m - 1].b;
     if (a_sc) q.flags |= RF_A_SCALAR;
     if (b_sc) q.flags |= RF_B_SCALAR;
+    // vector path: inner size a multiple of 4, every operand either a per-row
+    // value (inner stride 0) or 4-aligned rows of unit inner stride
     auto opnd_vec = [&](bool sc, uint64_t ptr, int64_t srow, int64_t sin, int e) {
       if (sc || sin == 0) return true;
       if (sin != 1) return false;
-      return al16(ptr) && (R == 1 || ((srow * e) & 15) == 0);
+      return al4(ptr, e) && (R == 1 || srow % 4 == 0);
     };
-    bool vec = (N % 8 == 0) && opnd_vec(false, q.o, q.so_row, 1, eo) &&
-               opnd_vec(a_sc, q.a, q.sa_row, q.sa_in, ea) &&
-               (!b || opnd_vec(b_sc, q.b, q.sb_row, q.sb_in, eb));
+    const bool vec = (N % 4 == 0) && opnd_vec(false, q.o, q.so_row, 1, eo) &&
+                     opnd_vec(a_sc, q.a, q.sa_row, q.sa_in, ea) &&
+                     (!b || opnd_vec(b_sc, q.b, q.sb_row, q.sb_in, eb));
     if (vec) q.flags |= RF_VEC;
     if (numel >= (1ll << 31) || N >= (1ll << 31)) {
       q.flags |= RF_BIG;
@@ -509,8 +525,8 @@ void build_ew(Pending& p, int op, bool is_slot, float p0, float p1,
       p.ext.so[i] = cd[i].o;
     }
   }
-  const int bpe = ea + eb + eo;
-  uint32_t ce = q.layout == EL_STRIDED ? 1024u : (bpe >= 10 ? 2048u : 4096u);
+  // provisional chunking; publish() resizes elementwise chunks per batch
+  const uint32_t ce = 2048u;
   q.chunk = ce;
   p.nchunk = (uint32_t)((numel + ce - 1) / ce);
   p.out_ext = extent_of(out);
@@ -734,7 +750,7 @@ void Executor::reclaim() {
   while (done_wm_ < next_seq_) {
     const uint64_t w = done_ring_[done_wm_ % kDoneRing];
     if ((w & kDoneMask) != done_wm_ + 1) break;
-    const uint32_t e = (uint32_t)(w >> 56);
+    const uint32_t e = (uint32_t)((w >> 48) & 0xffu);
     if (e) {
       ++errors_;
       if (err_seq_ == UINT64_MAX) err_seq_ = done_wm_;
@@ -818,22 +834,71 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       after_prev = lz;
     }
   }
+  // Elementwise chunk size for this batch: about two chunks per resident warp
+  // (multiple of 512 elements, 512..8192), half of that for the
+  // transcendental operators, whose chunks take longer.
+  uint64_t ew_elems = 0;
+  for (uint32_t r = 0; r < n; ++r)
+    if (reqs[i + r].r.kind == RK_EW) ew_elems += (uint64_t)reqs[i + r].r.numel;
+  const uint64_t warps = (uint64_t)std::max(1, total_warps_);
+  uint64_t ce = align_up(std::max<uint64_t>(1, ew_elems / (2 * warps)), 512);
+  ce = std::min<uint64_t>(std::max<uint64_t>(ce, 512), 8192);
+  std::vector<int> var(n);
+  for (uint32_t r = 0; r < n; ++r) {
+    Pending& p = reqs[i + r];
+    int v = p.r.op;
+    if (p.r.flags & RF_SLOT) {
+      const int s = p.r.op;
+      const int phys = (s >= 0 && s < kMaxSlots) ? tab_.alias[s] : -1;
+      v = (phys >= 0 && phys < kMaxSlots) ? tab_.slot[phys].variant : V_NONE;
+    }
+    var[r] = v;
+    if (p.r.kind != RK_EW) continue;
+    uint64_t c = is_heavy(v) ? std::max<uint64_t>(512, ce / 2) : ce;
+    if (p.r.layout == EL_STRIDED) c = std::min<uint64_t>(c, 2048);
+    // aligned chunks are staged through shared memory in units of unit_elems_
+    if ((p.r.flags & RF_VEC) && p.r.layout != EL_STRIDED) c = (uint64_t)unit_elems_;
+    p.r.chunk = (uint32_t)c;
+    p.nchunk = (uint32_t)(((uint64_t)p.r.numel + c - 1) / c);
+  }
+  // Within each stage the order of requests is free: group them by operator
+  // so that the warps of an SM run few operator bodies at a time.
+  std::vector<uint32_t> order(n);
+  for (uint32_t r = 0; r < n; ++r) order[r] = r;
+  for (uint32_t s0 = 0; s0 < n;) {
+    uint32_t s1 = s0 + 1;
+    while (s1 < n && stage_first[s1] == stage_first[s0]) ++s1;
+    std::stable_sort(order.begin() + s0, order.begin() + s1, [&](uint32_t x, uint32_t y) {
+      const int kx = reqs[i + x].r.kind * 1024 + var[x], ky = reqs[i + y].r.kind * 1024 + var[y];
+      return kx < ky;
+    });
+    s0 = s1;
+  }
   // payload layout
   std::vector<uint32_t> cb(n + 1);
   uint64_t nchunk = 0, floats = 0, counters = 0;
   uint32_t next = 0;
   for (uint32_t r = 0; r < n; ++r) {
+    const Pending& p = reqs[i + order[r]];
     cb[r] = (uint32_t)nchunk;
-    nchunk += reqs[i + r].nchunk;
-    floats += reqs[i + r].partials;
-    counters += reqs[i + r].counters;
-    if (reqs[i + r].has_ext) ++next;
+    nchunk += p.nchunk;
+    floats += p.partials;
+    counters += p.counters;
+    if (p.has_ext) ++next;
   }
   cb[n] = (uint32_t)nchunk;
   if (nchunk > 0xffffffffull) throw GError(GPUOS_EINVAL, "batch too large");
+  // Granules: the unit of work a CTA's producer takes at a time.  About four
+  // per pipeline CTA, at most 8 chunks each (one round of the producer warp).
+  const uint64_t nctas = (uint64_t)std::max(
+      1, opt_.mode == GPUOS_MODE_PERSISTENT ? grid_ - 1 : sm_count_ * batch_bps_);
+  uint64_t gran = nchunk / (4 * nctas);
+  gran = std::min<uint64_t>(std::max<uint64_t>(gran, 1), 8);
+  const uint64_t ngran = (nchunk + gran - 1) / gran;
   const uint64_t rec_off = 128;
   const uint64_t cb_off = rec_off + 128ull * n;
-  const uint64_t wait_off = cb_off + 4ull * (n + 1);
+  const uint64_t gtab_off = cb_off + 4ull * (n + 1);
+  const uint64_t wait_off = gtab_off + 4ull * ngran;
   const uint64_t ext_off = align_up(wait_off + (staged ? 4ull * n : 0), 16);
   const uint64_t bytes = align_up(ext_off + sizeof(ExtRec) * (uint64_t)next, 16);
   if (floats || counters) ensure_scratch_locked();
@@ -857,13 +922,14 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   h->scratch = floats ? reinterpret_cast<uint64_t>(partials_ + poff) : 0;
   h->counters = reinterpret_cast<uint64_t>(counters_);
   h->wait_from = done_wm_;
-  h->dev_off = (uint32_t)aoff;
+  h->gtab_off = (uint32_t)gtab_off;
+  h->gran = (uint32_t)gran;
   Req* recs = reinterpret_cast<Req*>(base + rec_off);
   uint32_t* cbp = reinterpret_cast<uint32_t*>(base + cb_off);
   ExtRec* ext = reinterpret_cast<ExtRec*>(base + ext_off);
   uint64_t pf = 0, pc = coff, xi = 0;
   for (uint32_t r = 0; r < n; ++r) {
-    Pending& p = reqs[i + r];
+    Pending& p = reqs[i + order[r]];
     Req q = p.r;
     if (p.has_ext) {
       ext[xi] = p.ext;
@@ -881,6 +947,15 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     recs[r] = q;
   }
   std::memcpy(cbp, cb.data(), 4ull * (n + 1));
+  {
+    uint32_t* gt = reinterpret_cast<uint32_t*>(base + gtab_off);
+    uint32_t r = 0;
+    for (uint64_t j = 0; j < ngran; ++j) {
+      const uint64_t c = j * gran;
+      while (r + 1 < n && cb[r + 1] <= c) ++r;
+      gt[j] = r;
+    }
+  }
   if (staged) {
     uint32_t* w = reinterpret_cast<uint32_t*>(base + wait_off);
     for (uint32_t r = 0; r < n; ++r) w[r] = stage_first[r] ? cb[stage_first[r]] : 0u;
@@ -907,8 +982,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       GCU(cudaStreamWaitEvent(stream, last_event_, 0));
     }
     GCU(cudaMemcpyAsync(ring_ + aoff, arena_ + aoff, bytes, cudaMemcpyHostToDevice, stream));
-    const int wpb = block_ / 32;
-    int grid = (int)std::min<uint64_t>((uint64_t)sm_count_ * batch_bps_, (nchunk + wpb - 1) / wpb);
+    int grid = (int)std::min<uint64_t>((uint64_t)sm_count_ * batch_bps_, ngran);
     grid = std::max(grid, 1);
     volatile uint64_t* dr = reinterpret_cast<volatile uint64_t*>(
         hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));

@@ -143,6 +143,8 @@ class Executor {
   int block_ = 512;
   int grid_ = 0;                // persistent worker grid (ingest CTA included)
   int batch_bps_ = 1;           // stream kernel: resident blocks per SM
+  int total_warps_ = 1;         // warps that execute a batch (chunk sizing)
+  int unit_elems_ = 2048;       // elements per staged elementwise chunk
   uint64_t idle_ns_ = 0, wait_limit_ns_ = 0;
   double sync_timeout_s_ = 60.0;
 
@@ -206,6 +208,7 @@ void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
 
 // helpers shared with the tests of the host logic
 uint32_t fdiv_magic(uint32_t d, uint32_t* shift);
+bool is_heavy(int variant);
 int variant_by_name(const std::string& name);
 // Match an fp32 expression against the reference scheduler's expression
 // table; returns the variant (and parameters) or -1.

@@ -211,10 +211,11 @@ def test_every_operator(op):
                     e.binary(s, ga, gb, go)
                 else:
                     e.unary(s, ga, go)
-                cases.append((a, b if binary else None, go, n, shift))
+                # the C ABI does not own tensors: keep the inputs alive until the flush
+                cases.append((a, b if binary else None, go, n, shift, ga, gb))
         e.flush(sync=True)
         p0, p1 = PARAMS.get(op, (0.0, 0.0))
-        for a, b, go, n, shift in cases:
+        for a, b, go, n, shift, _, _ in cases:
             compare(op, a, b, go.cpu(), p0, p1, where=f" n={n} shift={shift}")
 
 
@@ -235,13 +236,14 @@ def test_dtype_casts_bit_exact(op, dts):
             if op == "div0":
                 b[::7] = 0
             go = torch.empty(n, dtype=do, device=DEV)
+            ga, gb = gpu(a), gpu(b)
             if op in oracle.BINARY:
-                e.binary(s, gpu(a), gpu(b), go)
+                e.binary(s, ga, gb, go)
             else:
-                e.unary(s, gpu(a), go)
-            cases.append((a, b if op in oracle.BINARY else None, go))
+                e.unary(s, ga, go)
+            cases.append((a, b if op in oracle.BINARY else None, go, ga, gb))
         e.flush(sync=True)
-        for a, b, go in cases:
+        for a, b, go, _, _ in cases:
             ref = torch.empty(go.shape, dtype=do)
             oracle.ew(op, a, b, ref, *PARAMS.get(op, (0.0, 0.0)))
             got = go.cpu()
@@ -252,10 +254,14 @@ def test_dtype_casts_bit_exact(op, dts):
 # --------------------------------------------------------------------------
 # broadcast, views, strided layouts
 # --------------------------------------------------------------------------
+_KEEP = []  # device inputs of requests not yet flushed (the C ABI does not own tensors)
+
+
 def run_one(e, op, a, b, out_shape, out_dtype=torch.float32, out=None, p=(0.0, 0.0)):
     s = slot_of(e, op)
     ga = gpu(a)
     gb = gpu(b) if b is not None else None
+    _KEEP.extend([ga, gb])
     go = out if out is not None else torch.empty(out_shape, dtype=out_dtype, device=DEV)
     if b is not None:
         e.binary(s, ga, gb, go)
@@ -279,6 +285,7 @@ def test_broadcast_layouts(ex):
         shape = torch.broadcast_shapes(x.shape, y.shape)
         outs.append((op, x, y, run_one(ex, op, x, y, shape)))
     ex.flush(sync=True)
+    _KEEP.clear()
     for op, x, y, go in outs:
         compare(op, x, y, go.cpu(), where=f" {tuple(x.shape)}x{tuple(y.shape)}")
 
@@ -290,7 +297,8 @@ def test_column_broadcast_is_torch_semantics(ex):
     a = torch.tensor(k["a"])
     c = torch.tensor(k["c"]).reshape(-1, 1)
     go = torch.empty(a.shape, device=DEV)
-    ex.builtin(C.OP_ADD, gpu(a), gpu(c), go)
+    ga, gc = gpu(a), gpu(c)
+    ex.builtin(C.OP_ADD, ga, gc, go)
     ex.flush(sync=True)
     assert go.cpu().tolist() == k["torch"]
     assert go.cpu().tolist() != k["reference"]
@@ -303,7 +311,8 @@ def test_strided_and_noncontiguous_out(ex):
     base_out = torch.empty(6, 4, 7, 5 * 2, device=DEV)
     go = base_out[..., ::2]                                           # strided output
     s = slot_of(ex, "mul")
-    ex.binary(s, gpu(x), gpu(y), go)
+    gx, gy = gpu(x), gpu(y)
+    ex.binary(s, gx, gy, go)
     ex.flush(sync=True)
     ref = torch.empty(6, 4, 7, 5)
     oracle.ew("mul", x, y, ref)
@@ -414,10 +423,11 @@ def test_reductions(ex, op, trans):
             if not keep:
                 out_shape = [d for i, d in enumerate(out_shape) if i not in [a % x.dim() for a in axes]]
             go = torch.empty(out_shape, dtype=dt, device=DEV)
-            ex.reduce(s, gpu(x), go, axes, keep)
-            pend.append((x, go, axes, keep))
+            gx = gpu(x)
+            ex.reduce(s, gx, go, axes, keep)
+            pend.append((x, go, axes, keep, gx))
     ex.flush(sync=True)
-    for x, go, axes, keep in pend:
+    for x, go, axes, keep, _ in pend:
         check_reduce(op, x, go.cpu(), axes, keep)
 
 
