@@ -57,11 +57,15 @@ def build_lib(force=False, verbose=False) -> Path:
     if force or _stale(kobj, [CSRC / "kernels.cu", *DEV_HEADERS]):
         _run([NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
               "-c", CSRC / "kernels.cu", "-o", kobj], verbose)
+    nobj = BUILD / "noalloc.o"
+    if force or _stale(nobj, [CSRC / "noalloc.cu", ROOT / "include" / "gpuos_b200.h", *DEV_HEADERS]):
+        _run([NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
+              "-c", CSRC / "noalloc.cu", "-o", nobj], verbose)
     if force or _stale(robj, [CSRC / "runtime.cpp", *HOST_HEADERS]):
         _run(["g++", "-std=c++17", "-O2", "-fPIC", "-Wall", "-Wno-unused-parameter",
               f"-I{CUDA_HOME / 'include'}", "-c", CSRC / "runtime.cpp", "-o", robj], verbose)
-    if force or _stale(LIB, [kobj, robj]):
-        _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, kobj, robj,
+    if force or _stale(LIB, [kobj, robj, nobj]):
+        _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, kobj, robj, nobj,
               "-Xlinker", "--no-undefined", "-lpthread", "-ldl", "-lrt"], verbose)
     return LIB
 

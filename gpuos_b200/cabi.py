@@ -80,6 +80,9 @@ SIGNATURES = {
                                                 P(Tensor), P(Tensor), P(Tensor), P(Plan)]),
     "gpuos_plan_reduce": (ctypes.c_int32, [ctypes.c_int32, P(Tensor), P(Tensor), P(ctypes.c_int32),
                                            ctypes.c_int32, ctypes.c_int32, P(Plan)]),
+    "gpuos_reduce_rows_noalloc": (ctypes.c_int32, [ctypes.c_int32, _VP, ctypes.c_int32,
+                                                   ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                   _VP, ctypes.c_int32, _VP]),
     "gpuos_match_expression": (ctypes.c_int32, [ctypes.c_char_p, ctypes.c_int32,
                                                 P(ctypes.c_int32), P(ctypes.c_float),
                                                 P(ctypes.c_float)]),

@@ -1339,6 +1339,12 @@ void Executor::shutdown() {
 using gpuos::Executor;
 using gpuos::GError;
 
+namespace gpuos {
+// Lets the other translation units of this library report a message through
+// gpuos_last_error().
+void set_last_error(const char* msg) { t_last_error = msg; }
+}  // namespace gpuos
+
 namespace {
 template <class F>
 int32_t guard(F&& f) {

@@ -213,6 +213,22 @@ int32_t gpuos_match_expression(const char* expr, int32_t arity, int32_t* variant
  * persistent_kernel.cu:216-230). */
 int32_t gpuos_get_stats(gpuos_executor* ex, gpuos_stats* out);
 
+/* Sum (variant = the "sum" operator) or mean ("mean") over the last dimension
+ * of the row-major tensor x[rows, cols] (row i at x + i * row_stride elements)
+ * into out[rows], on `stream` (a cudaStream_t; NULL = the legacy stream), for
+ * callers that cannot allocate device memory.  No counterpart in the
+ * reference.  It allocates nothing: rows longer than 8192 columns are split
+ * into segments whose partial sums use a 1 MiB static device array that every
+ * GPU loading this library holds until exit, so a call may split at most
+ * 65,536 rows into at most 196,608 (row, segment) pairs; larger calls return
+ * GPUOS_EINVAL.  The first call on a device (the current one) looks the array
+ * up once per device, so make it before any stream capture.  All calls share
+ * the array: calls that overlap on the GPU race.  Results are those of
+ * gpuos_submit_reduce on the same input. */
+int32_t gpuos_reduce_rows_noalloc(int32_t variant, const void* x, int32_t x_dtype, int64_t rows,
+                                  int64_t cols, int64_t row_stride, void* out, int32_t out_dtype,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif
