@@ -123,32 +123,45 @@ uint32_t fdiv_magic(uint32_t d, uint32_t* shift) {
 }
 
 bool IntervalSet::overlaps(const Extent& e) const {
-  if (e.empty() || m_.empty()) return false;
-  auto it = m_.upper_bound(e.lo);
-  if (it != m_.end() && it->first < e.hi) return true;
-  if (it != m_.begin()) {
-    --it;
-    if (it->second > e.lo) return true;
+  if (e.empty() || v_.empty()) return false;
+  if (e.hi <= v_.front().lo || e.lo >= v_.back().hi) return false;
+  // first extent whose hi is above e.lo: the only candidate below e.hi
+  size_t lo = 0, hi = v_.size();
+  while (lo < hi) {
+    const size_t mid = (lo + hi) >> 1;
+    if (v_[mid].hi <= e.lo) lo = mid + 1; else hi = mid;
   }
-  return false;
+  return lo < v_.size() && v_[lo].lo < e.hi;
 }
 
 void IntervalSet::add(Extent e) {
   if (e.empty()) return;
-  auto it = m_.upper_bound(e.lo);
-  if (it != m_.begin()) {
-    auto p = std::prev(it);
-    if (p->second >= e.lo) {
-      e.lo = p->first;
-      e.hi = std::max(e.hi, p->second);
-      it = m_.erase(p);
-    }
+  if (v_.empty() || e.lo > v_.back().hi) {
+    v_.push_back(e);
+    return;
   }
-  while (it != m_.end() && it->first <= e.hi) {
-    e.hi = std::max(e.hi, it->second);
-    it = m_.erase(it);
+  if (e.lo >= v_.back().lo) {  // touches or overlaps the last extent only
+    if (e.hi > v_.back().hi) v_.back().hi = e.hi;
+    return;
   }
-  m_.emplace(e.lo, e.hi);
+  // merge with every extent in [first with hi >= e.lo, last with lo <= e.hi]
+  size_t lo = 0, hi = v_.size();
+  while (lo < hi) {
+    const size_t mid = (lo + hi) >> 1;
+    if (v_[mid].hi < e.lo) lo = mid + 1; else hi = mid;
+  }
+  size_t end = lo;
+  while (end < v_.size() && v_[end].lo <= e.hi) {
+    e.lo = std::min(e.lo, v_[end].lo);
+    e.hi = std::max(e.hi, v_[end].hi);
+    ++end;
+  }
+  if (end == lo) {
+    v_.insert(v_.begin() + (ptrdiff_t)lo, e);
+  } else {
+    v_[lo] = e;
+    v_.erase(v_.begin() + (ptrdiff_t)lo + 1, v_.begin() + (ptrdiff_t)end);
+  }
 }
 
 bool RingAlloc::alloc(uint64_t size, uint64_t tag, uint64_t* off) {
@@ -1047,6 +1060,9 @@ uint64_t Executor::flush(bool sync, cudaStream_t stream) {
         publish(lk, reqs, i, j, stream);
         i = j;
       }
+      // hand the vector's capacity back so that the next requests do not regrow it
+      reqs.clear();
+      if (pending_.empty()) pending_.swap(reqs);
     }
     ticket = next_seq_;
   }

@@ -41,16 +41,21 @@ struct Extent {
   bool empty() const { return hi <= lo; }
 };
 
-// Disjoint union of extents with O(log n) overlap queries.
+// Disjoint union of extents: a sorted flat vector of [lo, hi) with touching
+// extents merged.  Extents below or above everything held (the usual case for
+// slab-allocated tensors, which arrive in address order) are answered and
+// appended in O(1); others take a binary search.  clear() keeps the capacity,
+// so a warmed-up set does not allocate.
 class IntervalSet {
  public:
   bool overlaps(const Extent& e) const;
   void add(Extent e);
-  void clear() { m_.clear(); }
-  bool empty() const { return m_.empty(); }
+  void clear() { v_.clear(); }
+  bool empty() const { return v_.empty(); }
+  size_t size() const { return v_.size(); }
 
  private:
-  std::map<uint64_t, uint64_t> m_;  // lo -> hi
+  std::vector<Extent> v_;
 };
 
 // FIFO ring allocator: allocations are freed in allocation order.
