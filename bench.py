@@ -212,18 +212,23 @@ def flush_latency(ext, dev, reps=400):
 
 
 def roofline_leg(stream, dev, steps, peak_gbs, peak_kind):
-    """Per-launch CUDA-event timing of the batch kernel (stream mode)."""
-    import gpuos_b200
+    """Per-launch CUDA-event timing of the batch kernel (stream mode).
+
+    Each step's requests are queued first; the stream is then held by a short
+    spin kernel while one flush publishes the step's batches (512 requests
+    each, as in the main run), so that the launches run back to back and each
+    event pair around a launch times the kernel, not the host's launch latency.
+    """
     import gpuos_b200.cabi as C
     from gpuos_b200 import workloads as W
-    ex = C.Executor(torch.cuda.current_device(), mode=C.MODE_STREAM)
+    fe = stream.flush_every
+    ex = C.Executor(torch.cuda.current_device(), mode=C.MODE_STREAM, max_batch=fe)
     try:
         din, dout = stream.device_buffers(dev)
         views = stream.views(din, dout)
         # the same routing as the Python API, bound to this executor
         sub = W.Submitter(_CabiExt(ex))
         calls = sub.prepare(stream, views)
-        fe = stream.flush_every
         batch_bytes = []
         for i in range(0, len(stream.requests), fe):
             batch_bytes.append(sum(r.algo_bytes for r in stream.requests[i:i + fe]))
@@ -232,10 +237,10 @@ def roofline_leg(stream, dev, steps, peak_gbs, peak_kind):
         for s in range(steps + 1):
             if s == 1:
                 ex.take_timings()
-            for i, (fn, a) in enumerate(calls):
+            for fn, a in calls:
                 fn(*a)
-                if (i + 1) % fe == 0:
-                    ex.flush(sync=False, stream=cs)
+            torch.cuda._sleep(8_000_000)  # a few ms: longer than publishing the step
+            ex.flush(sync=False, stream=cs)
             ex.flush(sync=True, stream=cs)
         ms = ex.take_timings()
         per = len(batch_bytes)

@@ -29,7 +29,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIB = HERE / "libgpuos_b200.so"
 EXT = HERE / ("gpuos_ext" + sysconfig.get_config_var("EXT_SUFFIX"))
 
-DEV_HEADERS = [CSRC / "gpuos_abi.h", CSRC / "ops.cuh", CSRC / "executor.cuh", CSRC / "pipeline.cuh"]
+DEV_HEADERS = [CSRC / "gpuos_abi.h", CSRC / "ops.cuh", CSRC / "executor.cuh", CSRC / "batch.cuh"]
 HOST_HEADERS = [CSRC / "gpuos_abi.h", CSRC / "runtime.h", ROOT / "include" / "gpuos_b200.h"]
 
 

@@ -1,0 +1,208 @@
+// Batch execution on warps: every warp of the grid works through its share of
+// a batch's chunks straight from HBM, with no staging or hand-off between
+// warps.
+//
+//  * The host cuts each request into chunks and the batch into granules of
+//    `gran` consecutive chunks; for every granule it stores the request that
+//    owns the granule's first chunk (and that request's first chunk).  Warp g of W takes granules g, g + W, ...
+//    (no atomics), walks forward through the requests of its granules, and
+//    decodes each request's record once.
+//  * Aligned elementwise chunks run the vector body (ew_vec: 128-bit loads,
+//    up to 8 groups of 4 elements per lane in flight); strided views and
+//    reductions run the general warp bodies of executor.cuh.
+//  * Completion: each warp fences its stores, the CTA adds its chunk count to
+//    the batch's done counter once, and the CTA that completes the batch posts
+//    the completion word.  The last CTA to leave the batch marks its payload
+//    reusable (retired).
+//  * A batch with stage barriers (a request that depends on an earlier one)
+//    hands granules out in order with an atomic instead, counts chunks one by
+//    one, and a chunk of a later stage waits (bounded) until every chunk of
+//    the earlier stages is done.  Claims in order mean that an earlier stage
+//    is always held by a running warp, whether or not the grid is resident.
+//
+// Every wait is bounded by %globaltimer.
+#pragma once
+#include "executor.cuh"
+
+namespace gpuos {
+
+static constexpr int kWarpsPerCta = 8;
+static constexpr int kCtaThreads = 32 * kWarpsPerCta;
+static constexpr int kMinCtasPerSm = 2;
+
+struct CtaSmem {
+  ExtRec ext[kWarpsPerCta];  // per warp: the strided request's dims and strides
+  BatchHdr hdr;              // persistent worker: the current batch's header
+  uint32_t chunks;           // chunks this CTA finished in the current batch
+  int32_t go;                // persistent worker: a batch is ready
+  uint32_t off;              // persistent worker: its offset in the arena
+  uint32_t pad;
+};
+
+// The decoded request a warp is working on: the vector view of an aligned
+// elementwise request, or just its record for the other kinds (reloaded per
+// chunk, which keeps the vector path's registers free).
+struct Cur {
+  VecView u;
+  const Req* rec;
+  int v;
+  float p0, p1;
+  bool vec;
+};
+
+// The record carries the operator the request's slot named when it was
+// flushed (the host resolves the jump table), and its parameters.  A strided
+// request's ExtRec is copied from the arena to the warp's shared-memory slot.
+__device__ __forceinline__ void decode(Cur& cur, const Exec& ex, const Req* rec, ExtRec* xs) {
+  const ReqView q = load_req(rec, ex.lane);
+  cur.rec = rec;
+  cur.v = q.op == kOpNone ? V_NONE : q.op;
+  cur.p0 = q.p0;
+  cur.p1 = q.p1;
+  cur.vec = q.kind == RK_EW && (q.flags & RF_VEC) && q.layout != EL_STRIDED && ew_known(cur.v);
+  if (cur.vec) {
+    cur.u = vec_view(q);
+  } else if ((q.kind == RK_EW && q.layout == EL_STRIDED) ||
+             (q.kind == RK_RED && q.layout == RL_GENERIC)) {
+    static_assert(sizeof(ExtRec) % 16 == 0, "ExtRec is copied in 16-byte words");
+    const uint4* src = reinterpret_cast<const uint4*>(ex.base + q.ext);
+    uint4* dst = reinterpret_cast<uint4*>(xs);
+    for (uint32_t i = ex.lane; i < sizeof(ExtRec) / 16; i += 32) dst[i] = __ldcg(src + i);
+    __syncwarp();
+  }
+}
+
+__device__ __forceinline__ void run_chunk(const Exec& ex, const Cur& cur, uint32_t k,
+                                          const ExtRec* xs) {
+  if (cur.vec) {
+    const int64_t e0 = (int64_t)k * cur.u.chunk;
+    int64_t n = cur.u.numel - e0;
+    if (n > (int64_t)cur.u.chunk) n = cur.u.chunk;
+    ew_vec_dispatch(cur.v, cur.u, cur.p0, cur.p1, e0, n, ex.lane);
+  } else {
+    process_chunk(ex, load_req(cur.rec, ex.lane), cur.v, cur.p0, cur.p1, k, xs);
+  }
+}
+
+// One warp's share of a batch: warp gw of W.  Returns the chunks it ran that
+// are still to be counted (all of them, unless the batch counts chunk by chunk).
+__device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint32_t W,
+                                               ExtRec* xs) {
+  const int lane = ex.lane;
+  const uint32_t nchunk = ex.nchunk;
+  const bool staged = ex.flags & BF_STAGED;
+  const uint32_t G = ex.gran;
+  const uint32_t ngran = G ? (nchunk + G - 1) / G : 0u;
+  auto claim = [&]() -> uint32_t {
+    uint32_t x = 0;
+    if (lane == 0) x = atomicAdd(&ex.st->claim, 1u);
+    return __shfl_sync(GPUOS_FULL, x, 0);
+  };
+  uint32_t j = staged ? claim() : gw;
+  uint32_t count = 0, waited = 0;
+  int r = -1;
+  uint32_t rbase = 0, rend = 0;
+  Cur cur;
+  while (j < ngran) {
+    const uint32_t jn = staged ? claim() : j + W;  // the next granule, known ahead
+    uint32_t c = j * G;
+    const uint32_t cend = min(c + G, nchunk);
+    const uint2 g = __ldcg(ex.gtab + j);
+    if ((int)g.x != r) {
+      r = (int)g.x;
+      rbase = g.y;
+      rend = __ldcg(ex.gcb + r + 1);
+      decode(cur, ex, ex.recs + r, xs);
+    }
+    for (; c < cend; ++c) {
+      if (c >= rend) {
+        do {
+          ++r;
+          rbase = rend;
+          rend = __ldcg(ex.gcb + r + 1);
+        } while (c >= rend);
+        decode(cur, ex, ex.recs + r, xs);
+      }
+      if (staged) {
+        const uint32_t w = __ldcg(ex.req_wait + r);
+        if (w > waited) {
+          // every chunk of the earlier stages must be done first
+          if (lane == 0 && ld_acquire_u32(&ex.st->done) < w) {
+            const uint64_t t0 = globaltimer();
+            while (ld_acquire_u32(&ex.st->done) < w) {
+              __nanosleep(128);
+              if (globaltimer() - t0 > ex.wait_limit_ns) {
+                atomicOr(&ex.st->err, ERR_STAGE_TIMEOUT);
+                break;
+              }
+            }
+          }
+          waited = w;
+          __syncwarp();
+        }
+      }
+      run_chunk(ex, cur, c - rbase, xs);
+      if (staged) {
+        __threadfence();  // release this chunk's stores before it is counted
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t d = atomicAdd(&ex.st->done, 1u) + 1u;
+          if (d == nchunk) finish_batch(ex);
+        }
+      } else {
+        ++count;
+      }
+    }
+    j = jn;
+  }
+  return count;
+}
+
+// All threads of the CTA, after warp_batch: count the CTA's chunks into the
+// batch (completing it if they are the last), then leave the batch.  The last
+// of `nctas` CTAs to leave zeroes the batch's counters for the slot's next use
+// and, in the persistent worker, marks the payload reusable (retired); a
+// stream-mode payload is reusable once its kernel has completed.
+__device__ __forceinline__ void cta_leave_batch(const Exec& ex, uint32_t* cta_chunks,
+                                                uint32_t count, uint32_t nctas,
+                                                volatile uint64_t* retired_ring) {
+  __threadfence();  // each warp releases its stores
+  if (ex.lane == 0 && count) atomicAdd(cta_chunks, count);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t add = *cta_chunks;
+    *cta_chunks = 0;
+    if (add) {
+      const uint32_t d = atomicAdd(&ex.st->done, add) + add;
+      if (d == ex.nchunk) finish_batch(ex);
+    }
+    __threadfence();
+    const uint32_t left = atomicAdd(&ex.st->ctas_left, 1u) + 1u;
+    if (left == nctas) {
+      __threadfence();
+      ex.st->claim = 0;
+      ex.st->done = 0;
+      ex.st->err = 0;
+      ex.st->ctas_left = 0;
+      if (retired_ring) st_release_sys_u64(&retired_ring[ex.seq % kDoneRing], ex.seq + 1);
+    }
+  }
+  __syncthreads();
+}
+
+// Thread 0, before a batch with BF_AFTER_PREV: wait (bounded) until every
+// batch in [wait_from, seq) has completed.
+__device__ __forceinline__ void wait_prev_batches(const Exec& ex) {
+  const uint64_t t0 = globaltimer();
+  for (uint64_t j = ex.wait_from; j < ex.seq; ++j) {
+    while ((ld_acquire_u64(&ex.done_dev[j % kDoneRing]) & ((1ull << 48) - 1)) != j + 1) {
+      __nanosleep(256);
+      if (globaltimer() - t0 > ex.wait_limit_ns) {
+        atomicOr(&ex.st->err, ERR_STAGE_TIMEOUT);
+        return;
+      }
+    }
+  }
+}
+
+}  // namespace gpuos

@@ -27,8 +27,8 @@ namespace gpuos {
 #ifndef GPUOS_JIT_KNOWN
 #define GPUOS_JIT_KNOWN(v) false
 #endif
-#ifndef GPUOS_JIT_UNIT_CASES
-#define GPUOS_JIT_UNIT_CASES
+#ifndef GPUOS_JIT_VEC_CASES
+#define GPUOS_JIT_VEC_CASES
 #endif
 
 __device__ __forceinline__ bool ew_known(int v) {
@@ -86,12 +86,22 @@ __device__ __forceinline__ uint64_t u64of(uint32_t lo, uint32_t hi) {
   return ((uint64_t)hi << 32) | lo;
 }
 
-// Decode the 128-byte record from eight uniform 16-byte loads (L2, so that a
-// record restaged by the persistent worker is never read stale from L1).
-__device__ __forceinline__ ReqView load_req(const Req* g) {
-  const uint4* s = reinterpret_cast<const uint4*>(g);
-  const uint4 w0 = __ldcg(s + 0), w1 = __ldcg(s + 1), w2 = __ldcg(s + 2), w3 = __ldcg(s + 3);
-  const uint4 w4 = __ldcg(s + 4), w5 = __ldcg(s + 5), w6 = __ldcg(s + 6), w7 = __ldcg(s + 7);
+// Decode the 128-byte record (whole warp): lanes 0..7 read it as one
+// coalesced 128-byte load through L2 (the staging ring is rewritten for later
+// batches, so never from L1), and shuffles hand the words to every lane.
+__device__ __forceinline__ ReqView load_req(const Req* g, int lane) {
+  uint4 w = make_uint4(0u, 0u, 0u, 0u);
+  if (lane < 8) w = __ldcg(reinterpret_cast<const uint4*>(g) + lane);
+  auto word = [&](int i) {
+    uint4 r;
+    r.x = __shfl_sync(GPUOS_FULL, w.x, i);
+    r.y = __shfl_sync(GPUOS_FULL, w.y, i);
+    r.z = __shfl_sync(GPUOS_FULL, w.z, i);
+    r.w = __shfl_sync(GPUOS_FULL, w.w, i);
+    return r;
+  };
+  const uint4 w0 = word(0), w1 = word(1), w2 = word(2), w3 = word(3);
+  const uint4 w4 = word(4), w5 = word(5), w6 = word(6), w7 = word(7);
   ReqView q;
   q.op = (int)(w0.x & 0xffffu);
   q.kind = (int)((w0.x >> 16) & 0xffu);
@@ -131,42 +141,26 @@ __device__ __forceinline__ int64_t row_of(const ReqView& q, int64_t e) {
 // Execution context of one warp inside one batch.
 struct Exec {
   const uint8_t* base;          // batch payload in device memory
-  const BatchHdr* h;
   BatchState* st;
   const Req* recs;
+  const uint32_t* gcb;          // chunk prefix: first chunk of every request
+  const uint2* gtab;            // per granule: (request, that request's first chunk)
   const uint32_t* req_wait;     // per-request chunk count that must be done first (0: none)
-  const Tables* tab;
   float* scratch;               // partial sums of split reductions
   uint32_t* counters;           // self-cleaning combine counters
-  volatile uint64_t* done_ring; // completion words in mapped host memory (may be null)
+  volatile uint64_t* done_ring; // completion words in mapped host memory
   uint64_t* done_dev;           // device copy of the completion words (worker only)
   uint64_t wait_limit_ns;
   uint64_t seq;                 // batch sequence number
+  uint64_t wait_from;           // BF_AFTER_PREV: batches [wait_from, seq) first
   uint32_t nchunk;              // chunks in the batch
+  uint32_t gran;                // chunks per granule
+  uint32_t flags;               // BatchFlags
   int lane;
 };
 
 __device__ __forceinline__ void set_err(const Exec& ex, uint32_t bits) {
   atomicOr(&ex.st->err, bits);
-}
-
-// Jump-table resolution (alias -> physical slot -> variant + parameters).
-// The tables are read with plain volatile loads: the worker acquires at the
-// batch boundary, a launched kernel starts after the host's table writes.
-__device__ __forceinline__ int resolve(const ReqView& q, const Tables* tab, float& p0, float& p1) {
-  p0 = q.p0;
-  p1 = q.p1;
-  if (!(q.flags & RF_SLOT)) return q.op;
-  const int s = q.op;
-  if (s < 0 || s >= kMaxSlots) return V_NONE;
-  const volatile int32_t* al = tab->alias;
-  const int phys = al[s];
-  if (phys < 0 || phys >= kMaxSlots) return V_NONE;
-  const volatile SlotEntry* se = &tab->slot[phys];
-  const int v = se->variant;
-  p0 = se->p0;
-  p1 = se->p1;
-  return v;
 }
 
 // ---------------------------------------------------------------------------
@@ -192,13 +186,13 @@ __device__ __forceinline__ void ew_generic(const ReqView& q, const ExtRec* x, in
     } else {
       int64_t rem = e;
       oa = ob = oo = 0;
-      for (int d = __ldcg(&x->ndim) - 1; d >= 0; --d) {
-        const int64_t sz = __ldcg(&x->sizes[d]);
+      for (int d = x->ndim - 1; d >= 0; --d) {
+        const int64_t sz = x->sizes[d];
         const int64_t i = rem % sz;
         rem /= sz;
-        oa += i * __ldcg(&x->sa[d]);
-        ob += i * __ldcg(&x->sb[d]);
-        oo += i * __ldcg(&x->so[d]);
+        oa += i * x->sa[d];
+        ob += i * x->sb[d];
+        oo += i * x->so[d];
       }
     }
     const float A = ld1(q.a, q.dta, oa);
@@ -206,6 +200,201 @@ __device__ __forceinline__ void ew_generic(const ReqView& q, const ExtRec* x, in
     float R = 0.f;
     ew_apply1(v, A, B, R, p0, p1);
     st1(q.o, q.dto, oo, R);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Elementwise vector path: contiguous or row-strided requests whose pointers,
+// strides and row length are multiples of 4 elements (RF_VEC).  Each lane
+// handles groups of 4 adjacent elements; vec_groups<V>() groups per lane are
+// loaded (128-bit for fp32, 64-bit for fp16/bf16) before any is computed or
+// stored, so that a warp keeps 32 x groups x 16 bytes per operand in flight:
+// 8 groups for the light operators, 4 for the transcendental ones (whose
+// temporaries need the registers).
+// ---------------------------------------------------------------------------
+template <int V>
+__device__ __forceinline__ constexpr int vec_groups() {
+  return op_unroll<V>() == 2 ? 8 : 4;
+}
+
+enum OperandMode : int32_t { OM_LINEAR = 1, OM_ROW = 2, OM_ROWSPLAT = 3, OM_SCALAR = 4 };
+
+struct VecView {
+  uint64_t a, b, o;
+  int64_t numel, inner, sa_row, sb_row, so_row;
+  uint32_t chunk;
+  int ma, mb, dta, dtb, dto, flags;
+  bool rows, mo;
+  float As, Bs;
+  uint32_t fdiv_m, fdiv_s;
+};
+
+__device__ __forceinline__ VecView vec_view(const ReqView& q) {
+  VecView u;
+  const bool row2d = q.layout == EL_ROW2D;
+  auto mode = [&](bool scalar, int64_t srow, int64_t sin) -> int {
+    if (scalar) return OM_SCALAR;
+    if (!row2d) return OM_LINEAR;
+    if (sin == 0) return OM_ROWSPLAT;
+    return srow == q.inner ? OM_LINEAR : OM_ROW;
+  };
+  u.a = q.a; u.b = q.b; u.o = q.o;
+  u.numel = q.numel; u.chunk = q.chunk;
+  u.inner = q.inner; u.sa_row = q.sa_row; u.sb_row = q.sb_row; u.so_row = q.so_row;
+  u.ma = mode(q.flags & RF_A_SCALAR, q.sa_row, q.sa_in);
+  u.mb = (q.flags & RF_HAS_B) ? mode(q.flags & RF_B_SCALAR, q.sb_row, q.sb_in) : OM_SCALAR;
+  u.mo = row2d && q.so_row != q.inner;
+  u.rows = u.ma == OM_ROW || u.ma == OM_ROWSPLAT || u.mb == OM_ROW || u.mb == OM_ROWSPLAT || u.mo;
+  u.dta = q.dta; u.dtb = q.dtb; u.dto = q.dto; u.flags = q.flags;
+  u.fdiv_m = q.fdiv_m; u.fdiv_s = q.fdiv_s;
+  u.As = u.ma == OM_SCALAR ? ld1(q.a, q.dta, 0) : 0.f;
+  u.Bs = (u.mb == OM_SCALAR && (q.flags & RF_HAS_B)) ? ld1(q.b, q.dtb, 0) : 0.f;
+  return u;
+}
+
+__device__ __forceinline__ int64_t vec_row(const VecView& u, int64_t e) {
+  if (u.flags & RF_BIG) return e / u.inner;
+  return (int64_t)fdiv_u32((uint32_t)e, u.fdiv_m, u.fdiv_s);
+}
+
+__device__ __forceinline__ void vec_opnd4(int mode, uint64_t p, int dt, float sc, int64_t e,
+                                          int64_t rowoff, int64_t c, float* v) {
+  if (mode == OM_LINEAR) {
+    ld4(p, dt, e, v);
+  } else if (mode == OM_ROW) {
+    ld4(p, dt, rowoff + c, v);
+  } else if (mode == OM_ROWSPLAT) {
+    const float x = ld1(p, dt, rowoff);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = x;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = sc;
+  }
+}
+
+__device__ __forceinline__ float vec_opnd1(int mode, uint64_t p, int dt, float sc, int64_t e,
+                                           int64_t rowoff, int64_t c) {
+  if (mode == OM_LINEAR) return ld1(p, dt, e);
+  if (mode == OM_ROW) return ld1(p, dt, rowoff + c);
+  if (mode == OM_ROWSPLAT) return ld1(p, dt, rowoff);
+  return sc;
+}
+
+// elements [e0, e0 + n) of a request whose operands are all linear or scalar
+template <int V>
+__device__ __forceinline__ void ew_vec_flat(const VecView& u, float p0, float p1, int64_t e0,
+                                            int64_t n, int lane) {
+  constexpr int64_t kStep = 4 * 32;
+  constexpr int kG = vec_groups<V>();
+  const bool as = u.ma == OM_SCALAR, bs = u.mb == OM_SCALAR;
+  int64_t i = 4 * (int64_t)lane;
+  for (; i + kStep * (kG - 1) + 4 <= n; i += kStep * kG) {
+    float A[kG][4], B[kG][4];
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      const int64_t e = e0 + i + kStep * g;
+      if (as) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) A[g][k] = u.As;
+      } else {
+        ld4(u.a, u.dta, e, A[g]);
+      }
+      if (bs) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) B[g][k] = u.Bs;
+      } else {
+        ld4(u.b, u.dtb, e, B[g]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      float R[4];
+      op4<V>(A[g], B[g], R, p0, p1);
+      st4(u.o, u.dto, e0 + i + kStep * g, R);
+    }
+  }
+  for (; i < n; i += kStep) {
+    const int64_t e = e0 + i;
+    if (i + 4 <= n) {
+      float A[4], B[4], R[4];
+      vec_opnd4(u.ma, u.a, u.dta, u.As, e, 0, 0, A);
+      vec_opnd4(u.mb, u.b, u.dtb, u.Bs, e, 0, 0, B);
+      op4<V>(A, B, R, p0, p1);
+      st4(u.o, u.dto, e, R);
+    } else {
+      for (int64_t k = 0; k < n - i; ++k) {
+        const float A = vec_opnd1(u.ma, u.a, u.dta, u.As, e + k, 0, 0);
+        const float B = vec_opnd1(u.mb, u.b, u.dtb, u.Bs, e + k, 0, 0);
+        st1(u.o, u.dto, e + k, op1<V>(A, B, p0, p1));
+      }
+    }
+  }
+}
+
+// elements [e0, e0 + n) of a request with a per-row operand or output
+// (rows of u.inner elements, a multiple of 4)
+template <int V>
+__device__ __forceinline__ void ew_vec_rows(const VecView& u, float p0, float p1, int64_t e0,
+                                            int64_t n, int lane) {
+  constexpr int64_t kStep = 4 * 32;
+  constexpr int kG = 4;
+  int64_t i = 4 * (int64_t)lane;
+  for (; i + kStep * (kG - 1) + 4 <= n; i += kStep * kG) {
+    float A[kG][4], B[kG][4];
+    int64_t oo[kG];
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      const int64_t e = e0 + i + kStep * g;
+      const int64_t r = vec_row(u, e), c = e - r * u.inner;
+      vec_opnd4(u.ma, u.a, u.dta, u.As, e, r * u.sa_row, c, A[g]);
+      vec_opnd4(u.mb, u.b, u.dtb, u.Bs, e, r * u.sb_row, c, B[g]);
+      oo[g] = u.mo ? r * u.so_row + c : e;
+    }
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      float R[4];
+      op4<V>(A[g], B[g], R, p0, p1);
+      st4(u.o, u.dto, oo[g], R);
+    }
+  }
+  for (; i < n; i += kStep) {
+    const int64_t e = e0 + i;
+    if (i + 4 <= n) {
+      const int64_t r = vec_row(u, e), c = e - r * u.inner;
+      float A[4], B[4], R[4];
+      vec_opnd4(u.ma, u.a, u.dta, u.As, e, r * u.sa_row, c, A);
+      vec_opnd4(u.mb, u.b, u.dtb, u.Bs, e, r * u.sb_row, c, B);
+      op4<V>(A, B, R, p0, p1);
+      st4(u.o, u.dto, u.mo ? r * u.so_row + c : e, R);
+    } else {
+      // ragged end of a request: fewer than 4 elements
+      for (int64_t k = 0; k < n - i; ++k) {
+        const int64_t ek = e + k;
+        const int64_t r = vec_row(u, ek), c = ek - r * u.inner;
+        const float A = vec_opnd1(u.ma, u.a, u.dta, u.As, ek, r * u.sa_row, c);
+        const float B = vec_opnd1(u.mb, u.b, u.dtb, u.Bs, ek, r * u.sb_row, c);
+        st1(u.o, u.dto, u.mo ? r * u.so_row + c : ek, op1<V>(A, B, p0, p1));
+      }
+    }
+  }
+}
+
+template <int V>
+__device__ __forceinline__ void ew_vec(const VecView& u, float p0, float p1, int64_t e0, int64_t n,
+                                       int lane) {
+  if (u.rows) ew_vec_rows<V>(u, p0, p1, e0, n, lane);
+  else ew_vec_flat<V>(u, p0, p1, e0, n, lane);
+}
+
+#define GPUOS_VEC_CASE(V) case V: ew_vec<V>(u, p0, p1, e0, n, lane); return true;
+
+__device__ __forceinline__ bool ew_vec_dispatch(int v, const VecView& u, float p0, float p1,
+                                                int64_t e0, int64_t n, int lane) {
+  switch (v) {
+    GPUOS_ALL_EW(GPUOS_VEC_CASE)
+    GPUOS_JIT_VEC_CASES
+    default: return false;
   }
 }
 
@@ -381,22 +570,22 @@ __device__ __forceinline__ void red_generic(const Exec& ex, const ReqView& q, co
   const int64_t o0 = (int64_t)k * q.chunk;
   int64_t o1 = o0 + q.chunk;
   if (o1 > q.numel) o1 = q.numel;
-  const int nd = __ldcg(&x->ndim), rd = __ldcg(&x->rdim);
+  const int nd = x->ndim, rd = x->rdim;
   for (int64_t oi = o0 + ex.lane; oi < o1; oi += 32) {
     int64_t rem = oi, ib = 0, ob = 0;
     for (int d = nd - 1; d >= 0; --d) {
-      const int64_t sz = __ldcg(&x->sizes[d]);
+      const int64_t sz = x->sizes[d];
       const int64_t i = rem % sz;
       rem /= sz;
-      ib += i * __ldcg(&x->sa[d]);
-      ob += i * __ldcg(&x->so[d]);
+      ib += i * x->sa[d];
+      ob += i * x->so[d];
     }
     float acc = 0.f;
     for (int64_t rv = 0; rv < q.inner; ++rv) {
       int64_t t = rv, off = 0;
       for (int j = 0; j < rd; ++j) {
-        const int64_t sz = __ldcg(&x->rsizes[j]);
-        off += (t % sz) * __ldcg(&x->rstrides[j]);
+        const int64_t sz = x->rsizes[j];
+        off += (t % sz) * x->rstrides[j];
         t /= sz;
       }
       acc += ld1(q.a, q.dta, ib + off);
@@ -408,9 +597,9 @@ __device__ __forceinline__ void red_generic(const Exec& ex, const ReqView& q, co
 // ---------------------------------------------------------------------------
 // One chunk of one request.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, uint32_t k) {
-  float p0, p1;
-  const int v = resolve(q, ex.tab, p0, p1);
+// `x` is the request's ExtRec, copied to shared memory (strided layouts only).
+__device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, int v, float p0,
+                                              float p1, uint32_t k, const ExtRec* x) {
   if (q.kind == RK_EW) {
     if (!ew_known(v)) {
       if (ex.lane == 0) set_err(ex, ERR_BAD_OP);
@@ -419,7 +608,7 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
     const int64_t e0 = (int64_t)k * q.chunk;
     int64_t e1 = e0 + q.chunk;
     if (e1 > q.numel) e1 = q.numel;
-    ew_generic(q, reinterpret_cast<const ExtRec*>(ex.base + q.ext), v, p0, p1, e0, e1, ex.lane);
+    ew_generic(q, x, v, p0, p1, e0, e1, ex.lane);
     return;
   }
   if (v != V_SUM && v != V_MEAN) {
@@ -429,64 +618,51 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
   const bool mean = (v == V_MEAN);
   if (q.layout == RL_ROWS) red_rows(ex, q, mean, k);
   else if (q.layout == RL_COLS) red_cols(ex, q, mean, k);
-  else red_generic(ex, q, reinterpret_cast<const ExtRec*>(ex.base + q.ext), mean, k);
+  else red_generic(ex, q, x, mean, k);
 }
 
-// Lane 0 waits (bounded) until `target` chunks of the batch are done.
-__device__ __forceinline__ bool wait_chunks_done(const Exec& ex, uint32_t target) {
-  uint32_t ok = 1;
-  if (ex.lane == 0) {
-    if (ld_acquire_u32(&ex.st->done) < target) {
-      const uint64_t t0 = globaltimer();
-      unsigned ns = 32;
-      while (ld_acquire_u32(&ex.st->done) < target) {
-        __nanosleep(ns);
-        if (ns < 1024) ns <<= 1;
-        if (globaltimer() - t0 > ex.wait_limit_ns) { ok = 0; break; }
-      }
-    }
-  }
-  ok = __shfl_sync(GPUOS_FULL, ok, 0);
-  return ok != 0;
-}
-
-// Called by the warp that finished the last chunk of the batch.  The
-// completion word is seq + 1 with the batch's error bits in bits 48..55.
+// Called by the thread that counted the last chunk of the batch.  The
+// completion word is seq + 1 with the batch's error bits in bits 48..55.  The
+// persistent worker publishes it to the device ring (for batches that wait on
+// this one) and, with system scope, to the host.  A stream-mode batch is
+// complete when the event recorded after its launch is; the kernel writes the
+// word to the host only when the batch has an error (the host reads it after
+// that event, which makes the kernel's writes visible), so that a clean batch
+// ends without a write over PCIe.
 __device__ __forceinline__ void finish_batch(const Exec& ex) {
   __threadfence();
-  ex.st->t_last = globaltimer();
   const uint64_t seq = ex.seq;
   const uint32_t err = atomicOr(&ex.st->err, 0u);
   const uint64_t word = (seq + 1) | ((uint64_t)(err & 0xffu) << 48);
-  if (ex.done_dev) st_release_gpu_u64(&ex.done_dev[seq % kDoneRing], word);
-  if (ex.done_ring) {
-    __threadfence_system();
+  if (ex.done_dev) {
+    st_release_gpu_u64(&ex.done_dev[seq % kDoneRing], word);
     st_release_sys_u64(&ex.done_ring[seq % kDoneRing], word);
+  } else if (err) {
+    ex.done_ring[seq % kDoneRing] = word;
   }
 }
 
-// Bind the execution context of one batch payload.
-__device__ __forceinline__ Exec bind_batch(const uint8_t* payload, const Tables* tab,
-                                           volatile uint64_t* done_ring, uint64_t* done_dev,
-                                           uint64_t wait_limit_ns) {
-  // the header is read through L2: the persistent worker reuses payload memory
-  const BatchHdr* h = reinterpret_cast<const BatchHdr*>(payload);
+// Bind the execution context of one batch: its payload in the device staging
+// ring, a copy of its header (a kernel parameter, or shared memory in the
+// worker) and its device-side counters.
+__device__ __forceinline__ Exec bind_batch(const uint8_t* payload, const BatchHdr& h,
+                                           BatchState* st, volatile uint64_t* done_ring,
+                                           uint64_t* done_dev, uint64_t wait_limit_ns) {
   Exec ex;
   ex.base = payload;
-  ex.h = h;
-  ex.st = reinterpret_cast<BatchState*>(const_cast<uint8_t*>(payload) + sizeof(BatchHdr));
-  ex.recs = reinterpret_cast<const Req*>(payload + __ldcg(&h->rec_off));
-  const uint32_t flags = __ldcg(&h->flags);
-  const uint32_t gran = __ldcg(&h->gran), nch = __ldcg(&h->nchunk);
-  ex.req_wait = (flags & BF_STAGED)
-                    ? reinterpret_cast<const uint32_t*>(payload + __ldcg(&h->gtab_off)) +
-                          (nch + gran - 1) / gran
-                    : nullptr;
-  ex.tab = tab;
-  ex.scratch = reinterpret_cast<float*>(__ldcg(&h->scratch));
-  ex.counters = reinterpret_cast<uint32_t*>(__ldcg(&h->counters));
-  ex.seq = __ldcg(&h->seq);
-  ex.nchunk = __ldcg(&h->nchunk);
+  ex.st = st;
+  ex.recs = reinterpret_cast<const Req*>(payload + h.rec_off);
+  ex.gcb = reinterpret_cast<const uint32_t*>(payload + h.cb_off);
+  ex.gtab = reinterpret_cast<const uint2*>(payload + h.gtab_off);
+  ex.nchunk = h.nchunk;
+  ex.gran = h.gran;
+  ex.flags = h.flags;
+  const uint32_t ngran = h.gran ? (h.nchunk + h.gran - 1) / h.gran : 0u;
+  ex.req_wait = (h.flags & BF_STAGED) ? reinterpret_cast<const uint32_t*>(ex.gtab + ngran) : nullptr;
+  ex.scratch = reinterpret_cast<float*>(h.scratch);
+  ex.counters = reinterpret_cast<uint32_t*>(h.counters);
+  ex.seq = h.seq;
+  ex.wait_from = h.wait_from;
   ex.done_ring = done_ring;
   ex.done_dev = done_dev;
   ex.wait_limit_ns = wait_limit_ns;

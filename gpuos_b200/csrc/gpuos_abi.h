@@ -87,15 +87,19 @@ static constexpr int kMaxReqPerBatch = 4096;       // chunk prefix fits 16 KB of
 static constexpr int kWarpStep = 256;              // elements per warp step (8 per lane)
 
 // 128-byte request record.
+static constexpr uint16_t kOpNone = 0xffff;  // Req::op of a slot with no operator
+
 struct alignas(16) Req {
-  uint16_t op;           // variant id, or slot id if (flags & RF_SLOT)
+  uint16_t op;           // variant id, or slot id if (flags & RF_SLOT); a published record
+                         // always holds the variant (the host resolves the slot at flush),
+                         // kOpNone when the slot names no operator
   uint8_t  kind;         // ReqKind
   uint8_t  layout;       // EwLayout or RedLayout
   uint8_t  dta, dtb, dto;
   uint8_t  flags;        // ReqFlags
-  float    p0, p1;       // operator parameters (ignored for RF_SLOT: taken from the slot)
+  float    p0, p1;       // operator parameters (for RF_SLOT: taken from the slot at flush)
   // 16
-  uint32_t chunk;        // EW: elements per chunk (multiple of 256)
+  uint32_t chunk;        // EW: elements per chunk (a multiple of 4)
                          // RED: rows per chunk (nseg == 1) or columns per segment
   uint32_t nseg;         // RED: column segments per row group (1 = no combine)
   int64_t  numel;        // EW: output elements; RED: output rows
@@ -144,21 +148,20 @@ struct alignas(16) BatchHdr {
   uint64_t scratch;      // device address of this batch's partials area (floats)
   uint64_t counters;     // device address of the counter pool (u32, self-cleaning)
   uint64_t wait_from;    // BF_AFTER_PREV: batches [wait_from, seq) must be done first
-  uint32_t gtab_off;     // byte offset of uint32 gtab[ceil(nchunk / gran)]: request of
-                         // the first chunk of every granule
-  uint32_t gran;         // chunks per granule (the unit a producer takes at a time)
+  uint32_t gtab_off;     // byte offset of uint32x2 gtab[ceil(nchunk / gran)]: the request
+                         // that owns each granule's first chunk, and that request's
+                         // first chunk
+  uint32_t gran;         // chunks per granule (the unit a warp takes at a time)
 };
 static_assert(sizeof(BatchHdr) == 64, "BatchHdr must stay 64 bytes");
 
-// Per-batch device-side state (lives inside the device staging ring, right
-// after the payload copy; zeroed by whoever stages the batch).
+// Per-batch device-side counters: slot seq % kDoneRing of a device array,
+// zero at first use; the last CTA to leave a batch zeroes them again.
 struct alignas(16) BatchState {
-  uint32_t claim;        // next chunk index to hand out
+  uint32_t claim;        // next granule to hand out (batches with stage barriers)
   uint32_t done;         // chunks finished
-  uint32_t ctas_left;    // worker CTAs that left the batch
+  uint32_t ctas_left;    // CTAs that left the batch
   uint32_t err;          // ErrBits
-  uint64_t t_first;      // %globaltimer of the first claim
-  uint64_t t_last;       // %globaltimer when the last chunk finished
 };
 
 enum ErrBits : uint32_t {
@@ -166,6 +169,7 @@ enum ErrBits : uint32_t {
   ERR_BAD_KIND = 2,      // variant does not fit the request kind
   ERR_STAGE_TIMEOUT = 4, // a bounded wait for staging expired
   ERR_IDLE_EXIT = 8,
+  ERR_CUDA = 32,         // host-side: CUDA reported an error for the batch's launch
 };
 
 // Jump table: logical slot -> alias -> physical slot -> (variant, params).
@@ -231,10 +235,10 @@ struct alignas(64) DevCtrl {
 struct WorkerArgs {
   uint8_t* ring;                 // device staging ring
   const uint8_t* arena;          // device view of the pinned host arena
+  BatchState* states;            // device array of kDoneRing batch counters
   volatile HostCtrl* hctrl;      // device view of the host control block
   const volatile Pub* pub;       // device view of the publication ring
   DevCtrl* dctrl;                // device control block
-  const Tables* tab;
   volatile uint64_t* done_ring;
   volatile uint64_t* retired_ring;
   uint64_t start_seq;

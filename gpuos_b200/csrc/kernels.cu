@@ -2,35 +2,35 @@
 //
 //  gpuos_batch_kernel   one launch per batch, stream-ordered with the caller's
 //                       CUDA stream (the mode that interoperates with torch
-//                       streams and CUDA graphs).  One pipeline CTA per SM
-//                       (pipeline.cuh).
+//                       streams and CUDA graphs).  Every warp runs its share of
+//                       the batch's chunks (batch.cuh).
 //  gpuos_worker_kernel  the persistent worker: CTA 0 polls the doorbell in
 //                       mapped host memory and stages published batches into
-//                       the device ring; every other CTA is a pipeline that
-//                       walks the batches in order, its producer warp moving
-//                       from one batch to the next without draining.  Replaces
-//                       persistent_worker (src/persistent_kernel.cu:133-200),
-//                       whose thread 0 CAS-claims one 496-byte Task per CTA.
+//                       the device ring; every other CTA walks the staged
+//                       batches in order, its warps running their share of
+//                       each.  Replaces persistent_worker
+//                       (src/persistent_kernel.cu:133-200), whose thread 0
+//                       CAS-claims one 496-byte Task per CTA.
 //
 // Every wait in these kernels is bounded by %globaltimer.
-#include "pipeline.cuh"
+#include "batch.cuh"
 
 namespace gpuos {
 
-extern "C" __global__ void __launch_bounds__(kCtaThreads, 1)
-gpuos_batch_kernel(const uint8_t* payload, const Tables* tab, volatile uint64_t* done_ring,
-                   volatile uint64_t* retired_ring, uint64_t wait_limit_ns) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  PipeSmem* sm = pipe_init(smem);
-  uint8_t* bufs = smem + pipe_buf_offset();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == 0) {
-    Producer P{sm, bufs, 0, 0, wait_limit_ns, false};
-    produce_batch(P, payload, tab, nullptr, blockIdx.x, gridDim.x, lane);
-    produce_stop(P, lane);
-  } else {
-    consume(sm, bufs, tab, done_ring, nullptr, retired_ring, gridDim.x, wait_limit_ns);
-  }
+// The batch's descriptors are in the device staging ring (payload); its
+// counters are `st`, one slot of a device array.
+extern "C" __global__ void __launch_bounds__(kCtaThreads, kMinCtasPerSm)
+gpuos_batch_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
+                   volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
+  __shared__ ExtRec ext[kWarpsPerCta];
+  __shared__ uint32_t cta_chunks;
+  if (threadIdx.x == 0) cta_chunks = 0;
+  __syncthreads();
+  const Exec ex = bind_batch(payload, hdr, st, done_ring, nullptr, wait_limit_ns);
+  const int warp = threadIdx.x >> 5;
+  const uint32_t count = warp_batch(ex, blockIdx.x * kWarpsPerCta + warp,
+                                    gridDim.x * kWarpsPerCta, &ext[warp]);
+  cta_leave_batch(ex, &cta_chunks, count, gridDim.x, nullptr);
 }
 
 // Copy `bytes` (multiple of 16, both ends 16-byte aligned) from mapped host
@@ -113,28 +113,20 @@ __device__ void ingest_loop(const WorkerArgs& w) {
   }
 }
 
-// CTAs 1..n: a pipeline over the staged batches, in order.
-__device__ void pipeline_loop(const WorkerArgs& w, uint8_t* smem) {
-  PipeSmem* sm = pipe_init(smem);
-  uint8_t* bufs = smem + pipe_buf_offset();
+// CTAs 1..n: run the staged batches in order.
+__device__ __forceinline__ void worker_loop(const WorkerArgs& w, CtaSmem* sm) {
   const uint32_t nproc = gridDim.x - 1;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t gw = (blockIdx.x - 1) * kWarpsPerCta + (threadIdx.x >> 5);
   // the ingest stops the worker after idle_ns without work, so waiting much
   // longer than that for the next batch means it is gone
   const uint64_t idle_limit = w.idle_ns + 2000000000ull;
-  if (warp != 0) {
-    consume(sm, bufs, w.tab, w.done_ring, w.dctrl->done_dev, w.retired_ring, nproc,
-            idle_limit + w.wait_limit_ns);
-    return;
-  }
-  Producer P{sm, bufs, 0, 0, w.wait_limit_ns, false};
+  if (threadIdx.x == 0) sm->chunks = 0;
   for (uint64_t s = w.start_seq;; ++s) {
-    int go = 0;
-    uint32_t off = 0;
-    if (lane == 0) {
+    if (threadIdx.x == 0) {
+      int go = 0;
       const uint64_t t0 = globaltimer();
       unsigned backoff = 32;
-      while (!P.dead) {
+      while (true) {
         if (ld_acquire_u64(&w.dctrl->ready) > s) { go = 1; break; }
         if (ld_acquire_u64(&w.dctrl->stop_at) <= s) break;
         if (globaltimer() - t0 > idle_limit) {
@@ -144,68 +136,61 @@ __device__ void pipeline_loop(const WorkerArgs& w, uint8_t* smem) {
         __nanosleep(backoff);
         if (backoff < 2048) backoff <<= 1;
       }
-      if (go) off = *reinterpret_cast<volatile uint32_t*>(&w.dctrl->ready_off[s % kDoneRing]);
+      sm->go = go;
+      if (go) sm->off = *reinterpret_cast<volatile uint32_t*>(&w.dctrl->ready_off[s % kDoneRing]);
     }
-    go = __shfl_sync(GPUOS_FULL, go, 0);
-    off = __shfl_sync(GPUOS_FULL, off, 0);
-    if (!go) break;
-    produce_batch(P, w.ring + off, w.tab, w.dctrl->done_dev, blockIdx.x - 1, nproc, lane);
-    const int dead = __shfl_sync(GPUOS_FULL, P.dead ? 1 : 0, 0);
-    if (dead) break;
+    __syncthreads();
+    if (!sm->go) return;
+    const uint8_t* payload = w.ring + sm->off;
+    if (threadIdx.x < sizeof(BatchHdr) / 16) {
+      // the header through L2: the ring is reused, and the ingest CTA wrote it
+      reinterpret_cast<uint4*>(&sm->hdr)[threadIdx.x] =
+          __ldcg(reinterpret_cast<const uint4*>(payload) + threadIdx.x);
+    }
+    __syncthreads();
+    const Exec ex = bind_batch(payload, sm->hdr, &w.states[s % kDoneRing], w.done_ring,
+                               w.dctrl->done_dev, w.wait_limit_ns);
+    if (threadIdx.x == 0 && (ex.flags & BF_AFTER_PREV)) wait_prev_batches(ex);
+    __syncthreads();
+    const uint32_t count = warp_batch(ex, gw, nproc * kWarpsPerCta, &sm->ext[threadIdx.x >> 5]);
+    cta_leave_batch(ex, &sm->chunks, count, nproc, w.retired_ring);
   }
-  produce_stop(P, lane);
 }
 
-extern "C" __global__ void __launch_bounds__(kCtaThreads, 1) gpuos_worker_kernel(WorkerArgs w) {
-  extern __shared__ __align__(128) uint8_t smem[];
+extern "C" __global__ void __launch_bounds__(kCtaThreads, kMinCtasPerSm)
+gpuos_worker_kernel(WorkerArgs w) {
+  __shared__ CtaSmem sm;
   if (blockIdx.x == 0) ingest_loop(w);
-  else pipeline_loop(w, smem);
+  else worker_loop(w, &sm);
 }
 
 }  // namespace gpuos
 
 // ---- launch wrappers used by the host runtime ------------------------------
-extern "C" size_t gpuos_pipe_smem_bytes() { return gpuos::pipe_smem_bytes(); }
 extern "C" int gpuos_cta_threads() { return gpuos::kCtaThreads; }
-extern "C" int gpuos_unit_elems() { return gpuos::kUnit; }
 
-// Opt in to the dynamic shared memory of a pipeline CTA (current device).
-extern "C" cudaError_t gpuos_kernel_setup() {
-  const int bytes = (int)gpuos::pipe_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(gpuos::gpuos_batch_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(gpuos::gpuos_worker_kernel,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-}
-
-extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::Tables* tab,
-                                          volatile uint64_t* done_ring,
-                                          volatile uint64_t* retired_ring, uint64_t wait_limit_ns,
-                                          int grid, int block, cudaStream_t stream) {
-  (void)block;
-  gpuos::gpuos_batch_kernel<<<grid, gpuos::kCtaThreads, gpuos::pipe_smem_bytes(), stream>>>(
-      payload, tab, done_ring, retired_ring, wait_limit_ns);
+extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::BatchHdr* hdr,
+                                          gpuos::BatchState* st, volatile uint64_t* done_ring,
+                                          uint64_t wait_limit_ns, int grid, cudaStream_t stream) {
+  gpuos::gpuos_batch_kernel<<<grid, gpuos::kCtaThreads, 0, stream>>>(payload, *hdr, st, done_ring,
+                                                                     wait_limit_ns);
   return cudaGetLastError();
 }
 
-extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, int block,
-                                           cudaStream_t stream) {
-  (void)block;
+extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, cudaStream_t stream) {
   const gpuos::WorkerArgs* w = static_cast<const gpuos::WorkerArgs*>(args);
-  gpuos::gpuos_worker_kernel<<<grid, gpuos::kCtaThreads, gpuos::pipe_smem_bytes(), stream>>>(*w);
+  gpuos::gpuos_worker_kernel<<<grid, gpuos::kCtaThreads, 0, stream>>>(*w);
   return cudaGetLastError();
 }
 
-extern "C" cudaError_t gpuos_occupancy(int block, int* batch_blocks_per_sm,
-                                       int* worker_blocks_per_sm) {
-  (void)block;
-  const size_t smem = gpuos::pipe_smem_bytes();
+// Resident blocks per SM of the two kernels (the persistent grid must be
+// fully resident).
+extern "C" cudaError_t gpuos_occupancy(int* batch_blocks_per_sm, int* worker_blocks_per_sm) {
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      batch_blocks_per_sm, gpuos::gpuos_batch_kernel, gpuos::kCtaThreads, smem);
+      batch_blocks_per_sm, gpuos::gpuos_batch_kernel, gpuos::kCtaThreads, 0);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      worker_blocks_per_sm, gpuos::gpuos_worker_kernel, gpuos::kCtaThreads, smem);
+      worker_blocks_per_sm, gpuos::gpuos_worker_kernel, gpuos::kCtaThreads, 0);
 }
 
 extern "C" size_t gpuos_worker_args_size() { return sizeof(gpuos::WorkerArgs); }

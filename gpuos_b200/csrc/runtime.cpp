@@ -19,17 +19,12 @@
 #define GPUOS_PAUSE() std::this_thread::yield()
 #endif
 
-extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::Tables* tab,
-                                          volatile uint64_t* done_ring,
-                                          volatile uint64_t* retired_ring, uint64_t wait_limit_ns,
-                                          int grid, int block, cudaStream_t stream);
-extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, int block,
-                                           cudaStream_t stream);
-extern "C" cudaError_t gpuos_occupancy(int block, int* batch_blocks_per_sm,
-                                       int* worker_blocks_per_sm);
-extern "C" cudaError_t gpuos_kernel_setup();
+extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::BatchHdr* hdr,
+                                          gpuos::BatchState* st, volatile uint64_t* done_ring,
+                                          uint64_t wait_limit_ns, int grid, cudaStream_t stream);
+extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, cudaStream_t stream);
+extern "C" cudaError_t gpuos_occupancy(int* batch_blocks_per_sm, int* worker_blocks_per_sm);
 extern "C" int gpuos_cta_threads();
-extern "C" int gpuos_unit_elems();
 
 namespace gpuos {
 
@@ -347,20 +342,17 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
 
   GCU(cudaFree(nullptr));
   GCU(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, device));
-  GCU(gpuos_kernel_setup());
-  // The CTA shape is fixed by the kernels (one producer warp and eight
-  // consumer warps); threads_per_block is accepted for API compatibility.
+  // The CTA shape is fixed by the kernels (eight warps); threads_per_block is
+  // accepted for API compatibility.
   block_ = gpuos_cta_threads();
   int bbps = 0, wbps = 0;
-  GCU(gpuos_occupancy(block_, &bbps, &wbps));
-  if (bbps < 1 || wbps < 1) throw GError(GPUOS_ECUDA, "pipeline CTA cannot be resident");
+  GCU(gpuos_occupancy(&bbps, &wbps));
+  if (bbps < 1 || wbps < 2) throw GError(GPUOS_ECUDA, "batch CTAs cannot be resident");
   batch_bps_ = bbps;
-  // one pipeline CTA per SM; the persistent worker adds its ingest CTA in
-  // place of one of them
-  grid_ = sm_count_;
-  const int pipelines = opt_.mode == GPUOS_MODE_PERSISTENT ? grid_ - 1 : sm_count_ * batch_bps_;
-  total_warps_ = pipelines * 8;
-  unit_elems_ = gpuos_unit_elems();
+  // the persistent grid is fully resident: CTA 0 stages batches, the rest run them
+  grid_ = sm_count_ * wbps;
+  const int ctas = opt_.mode == GPUOS_MODE_PERSISTENT ? grid_ - 1 : sm_count_ * batch_bps_;
+  total_warps_ = ctas * gpuos_cta_threads() / 32;
 
   GCU(cudaStreamCreateWithFlags(&s_worker_, cudaStreamNonBlocking));
   GCU(cudaStreamCreateWithFlags(&s_ctrl_, cudaStreamNonBlocking));
@@ -372,6 +364,9 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   GCU(cudaHostAlloc(reinterpret_cast<void**>(&arena_), arena_bytes_, cudaHostAllocMapped));
   GCU(cudaHostGetDevicePointer(reinterpret_cast<void**>(&arena_dev_), arena_, 0));
   GCU(cudaMalloc(reinterpret_cast<void**>(&ring_), arena_bytes_));
+  // per-batch counters (self-cleaning; zero before first use)
+  GCU(cudaMalloc(reinterpret_cast<void**>(&states_), sizeof(BatchState) * kDoneRing));
+  GCU(cudaMemset(states_, 0, sizeof(BatchState) * kDoneRing));
   arena_alloc_.init(arena_bytes_);
 
   // host control block + rings
@@ -403,8 +398,6 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   }
   tab_.slot[0] = SlotEntry{V_ADD, 0.f, 0.f, 2};
   tab_.slot[1] = SlotEntry{V_MUL, 0.f, 0.f, 2};
-  GCU(cudaMalloc(reinterpret_cast<void**>(&tab_dev_), sizeof(Tables)));
-  upload_tables_locked();
   GCU(cudaDeviceSynchronize());
   started_ = true;
   if (opt_.mode == GPUOS_MODE_PERSISTENT) launch_worker_locked(0);
@@ -415,12 +408,6 @@ Executor::~Executor() {
     shutdown();
   } catch (...) {
   }
-}
-
-void Executor::upload_tables_locked() {
-  DeviceGuard g(device_);
-  GCU(cudaMemcpyAsync(tab_dev_, &tab_, sizeof(Tables), cudaMemcpyHostToDevice, s_ctrl_));
-  GCU(cudaStreamSynchronize(s_ctrl_));
 }
 
 void Executor::ensure_scratch_locked() {
@@ -760,6 +747,29 @@ void Executor::submit_task(const void* task) {
 
 // ---- batches ----------------------------------------------------------------
 void Executor::reclaim() {
+  if (opt_.mode == GPUOS_MODE_STREAM) {
+    // a batch is done once the event recorded after its launch has completed;
+    // the kernel posts a completion word only for a batch with errors
+    while (done_wm_ < next_seq_) {
+      const cudaError_t q = cudaEventQuery(done_ev_[done_wm_ % kDoneRing]);
+      if (q == cudaErrorNotReady) break;
+      uint32_t e = 0;
+      if (q != cudaSuccess) {
+        e = ERR_CUDA;
+        if (cuda_err_.empty()) cuda_err_ = cudaGetErrorString(q);
+      } else {
+        const uint64_t w = done_ring_[done_wm_ % kDoneRing];
+        e = (w & kDoneMask) == done_wm_ + 1 ? (uint32_t)((w >> 48) & 0xffu) : 0u;
+      }
+      if (e) {
+        ++errors_;
+        if (err_seq_ == UINT64_MAX) err_seq_ = done_wm_;
+        err_bits_ |= e;
+      }
+      ++done_wm_;
+    }
+    retired_wm_ = done_wm_;
+  }
   while (done_wm_ < next_seq_) {
     const uint64_t w = done_ring_[done_wm_ % kDoneRing];
     if ((w & kDoneMask) != done_wm_ + 1) break;
@@ -869,10 +879,12 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     if (p.r.kind != RK_EW) continue;
     uint64_t c = is_heavy(v) ? std::max<uint64_t>(512, ce / 2) : ce;
     if (p.r.layout == EL_STRIDED) c = std::min<uint64_t>(c, 2048);
-    // aligned chunks are staged through shared memory in units of unit_elems_
-    if ((p.r.flags & RF_VEC) && p.r.layout != EL_STRIDED) c = (uint64_t)unit_elems_;
+    // equal chunks (a multiple of 4 elements, as the vector path needs)
+    const uint64_t numel = (uint64_t)p.r.numel;
+    const uint64_t k = (numel + c - 1) / c;
+    c = align_up((numel + k - 1) / k, 4);
     p.r.chunk = (uint32_t)c;
-    p.nchunk = (uint32_t)(((uint64_t)p.r.numel + c - 1) / c);
+    p.nchunk = (uint32_t)((numel + c - 1) / c);
   }
   // Within each stage the order of requests is free: group them by operator
   // so that the warps of an SM run few operator bodies at a time.
@@ -901,17 +913,17 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   }
   cb[n] = (uint32_t)nchunk;
   if (nchunk > 0xffffffffull) throw GError(GPUOS_EINVAL, "batch too large");
-  // Granules: the unit of work a CTA's producer takes at a time.  About four
-  // per pipeline CTA, at most 8 chunks each (one round of the producer warp).
-  const uint64_t nctas = (uint64_t)std::max(
-      1, opt_.mode == GPUOS_MODE_PERSISTENT ? grid_ - 1 : sm_count_ * batch_bps_);
-  uint64_t gran = nchunk / (4 * nctas);
+  // Granules: the unit of work a warp takes at a time, about two per warp
+  // (at most 8 chunks each).
+  const uint64_t warps_all = (uint64_t)std::max(1, total_warps_);
+  uint64_t gran = nchunk / (2 * warps_all);
   gran = std::min<uint64_t>(std::max<uint64_t>(gran, 1), 8);
   const uint64_t ngran = (nchunk + gran - 1) / gran;
-  const uint64_t rec_off = 128;
+  const uint64_t rec_off = sizeof(BatchHdr);
   const uint64_t cb_off = rec_off + 128ull * n;
-  const uint64_t gtab_off = cb_off + 4ull * (n + 1);
-  const uint64_t wait_off = gtab_off + 4ull * ngran;
+  // the granule table is read as 8-byte pairs
+  const uint64_t gtab_off = align_up(cb_off + 4ull * (n + 1), 8);
+  const uint64_t wait_off = gtab_off + 8ull * ngran;
   const uint64_t ext_off = align_up(wait_off + (staged ? 4ull * n : 0), 16);
   const uint64_t bytes = align_up(ext_off + sizeof(ExtRec) * (uint64_t)next, 16);
   if (floats || counters) ensure_scratch_locked();
@@ -923,7 +935,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   if (!wait_for_room_locked(lk, bytes, floats, counters, &aoff, &poff, &coff, seq))
     throw GError(GPUOS_ETIMEOUT, "timed out waiting for staging memory");
   uint8_t* base = arena_ + aoff;
-  std::memset(base, 0, 128);
+  std::memset(base, 0, sizeof(BatchHdr));
   BatchHdr* h = reinterpret_cast<BatchHdr*>(base);
   h->seq = seq;
   h->nreq = n;
@@ -944,6 +956,18 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + order[r]];
     Req q = p.r;
+    // the operator (and parameters) the request's slot names now: the
+    // device runs the record as it stands
+    if (q.flags & RF_SLOT) {
+      const int s = q.op;
+      const int phys = (s >= 0 && s < kMaxSlots) ? tab_.alias[s] : -1;
+      if (phys >= 0 && phys < kMaxSlots) {
+        q.p0 = tab_.slot[phys].p0;
+        q.p1 = tab_.slot[phys].p1;
+      }
+      q.flags = (uint8_t)(q.flags & ~RF_SLOT);
+    }
+    q.op = var[order[r]] < 0 ? kOpNone : (uint16_t)var[order[r]];
     if (p.has_ext) {
       ext[xi] = p.ext;
       q.ext = (uint32_t)(ext_off + sizeof(ExtRec) * xi);
@@ -966,7 +990,8 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     for (uint64_t j = 0; j < ngran; ++j) {
       const uint64_t c = j * gran;
       while (r + 1 < n && cb[r + 1] <= c) ++r;
-      gt[j] = r;
+      gt[2 * j] = r;
+      gt[2 * j + 1] = cb[r];
     }
   }
   if (staged) {
@@ -990,17 +1015,16 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     ensure_worker_locked();
   } else {
     DeviceGuard g(device_);
-    if (last_stream_ && stream != last_stream_ && done_wm_ < seq) {
+    if (have_last_stream_ && stream != last_stream_ && done_wm_ < seq) {
       GCU(cudaEventRecord(last_event_, last_stream_));
       GCU(cudaStreamWaitEvent(stream, last_event_, 0));
     }
     GCU(cudaMemcpyAsync(ring_ + aoff, arena_ + aoff, bytes, cudaMemcpyHostToDevice, stream));
-    int grid = (int)std::min<uint64_t>((uint64_t)sm_count_ * batch_bps_, ngran);
+    const uint64_t wpc = (uint64_t)block_ / 32;
+    int grid = (int)std::min<uint64_t>((uint64_t)sm_count_ * batch_bps_, (ngran + wpc - 1) / wpc);
     grid = std::max(grid, 1);
     volatile uint64_t* dr = reinterpret_cast<volatile uint64_t*>(
         hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));
-    volatile uint64_t* rr = reinterpret_cast<volatile uint64_t*>(
-        hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(retired_ring_) - hostblk_));
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (timing_) {
       for (cudaEvent_t* e : {&e0, &e1}) {
@@ -1013,12 +1037,18 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       }
       GCU(cudaEventRecord(e0, stream));
     }
-    GCU(gpuos_launch_batch(ring_ + aoff, tab_dev_, dr, rr, wait_limit_ns_, grid, block_, stream));
+    GCU(gpuos_launch_batch(ring_ + aoff, h, states_ + seq % kDoneRing, dr, wait_limit_ns_, grid,
+                           stream));
     if (timing_) {
       GCU(cudaEventRecord(e1, stream));
       timed_.emplace_back(e0, e1);
     }
+    // completion (and the reuse of the batch's staging memory) is this event
+    cudaEvent_t& de = done_ev_[seq % kDoneRing];
+    if (!de) GCU(cudaEventCreateWithFlags(&de, cudaEventDisableTiming));
+    GCU(cudaEventRecord(de, stream));
     last_stream_ = stream;
+    have_last_stream_ = true;
   }
 }
 
@@ -1031,7 +1061,7 @@ uint64_t Executor::flush(bool sync, cudaStream_t stream) {
     reqs.swap(pending_);
     if (!reqs.empty()) {
       DeviceGuard g(device_);
-      if (!stream) stream = s_own_;
+      // stream NULL is CUDA's legacy default stream, as everywhere in CUDA
       if (opt_.mode == GPUOS_MODE_PERSISTENT && stream != s_own_) {
         // the worker reads the inputs as soon as the doorbell rings, so work
         // still queued on the producer stream must finish first
@@ -1086,6 +1116,7 @@ void Executor::wait(uint64_t ticket, double timeout_s) {
           if (e & ERR_BAD_OP) why += " a request used a slot with no registered operator;";
           if (e & ERR_BAD_KIND) why += " a slot's operator does not fit the request kind;";
           if (e & ERR_STAGE_TIMEOUT) why += " a stage barrier wait timed out;";
+          if (e & ERR_CUDA) why += " CUDA reported: " + cuda_err_ + ";";
           throw GError(GPUOS_EDEVICE, "gpuos batch error:" + why);
         }
         return;
@@ -1117,12 +1148,12 @@ void Executor::launch_worker_locked(uint64_t start) {
                       s_worker_));
   WorkerArgs w;
   w.ring = ring_;
+  w.states = states_;
   w.arena = arena_dev_;
   w.hctrl = reinterpret_cast<volatile HostCtrl*>(hostblk_dev_);
   w.pub = reinterpret_cast<const volatile Pub*>(
       hostblk_dev_ + (reinterpret_cast<uint8_t*>(pub_) - hostblk_));
   w.dctrl = dctrl_;
-  w.tab = tab_dev_;
   w.done_ring = reinterpret_cast<volatile uint64_t*>(
       hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));
   w.retired_ring = reinterpret_cast<volatile uint64_t*>(
@@ -1130,7 +1161,7 @@ void Executor::launch_worker_locked(uint64_t start) {
   w.start_seq = start;
   w.wait_limit_ns = wait_limit_ns_;
   w.idle_ns = idle_ns_;
-  GCU(gpuos_launch_worker(&w, grid_, block_, s_worker_));
+  GCU(gpuos_launch_worker(&w, grid_, s_worker_));
   worker_launched_ = true;
   ++relaunches_;
 }
@@ -1184,7 +1215,6 @@ int Executor::register_elementwise(const std::string& key, const std::string& ex
   if (next_slot_ >= kMaxSlots) throw GError(GPUOS_EINVAL, "jump table is full (128 slots)");
   const int slot = next_slot_++;
   tab_.slot[slot] = SlotEntry{v, p0, p1, arity};
-  upload_tables_locked();
   slot_of_key_.emplace(key, slot);
   return slot;
 }
@@ -1200,7 +1230,6 @@ int Executor::register_reduce(const std::string& key, const std::string& op_name
   if (next_slot_ >= kMaxSlots) throw GError(GPUOS_EINVAL, "jump table is full (128 slots)");
   const int slot = next_slot_++;
   tab_.slot[slot] = SlotEntry{v, 0.f, 0.f, 1};
-  upload_tables_locked();
   slot_of_key_.emplace(key, slot);
   return slot;
 }
@@ -1210,7 +1239,6 @@ void Executor::set_alias(int logical, int physical) {
     throw GError(GPUOS_EINVAL, "slot out of range");
   std::lock_guard<std::mutex> lk(mu_);
   tab_.alias[logical] = physical;
-  upload_tables_locked();
 }
 
 void Executor::set_slot(int slot, int variant, float p0, float p1) {
@@ -1223,7 +1251,6 @@ void Executor::set_slot(int slot, int variant, float p0, float p1) {
                      variant == V_DIV0 || variant == V_DIV || variant == V_MAX ||
                      variant == V_MIN || variant == V_POW) ? 2 : 1;
   tab_.slot[slot] = SlotEntry{variant, p0, p1, arity};
-  upload_tables_locked();
 }
 
 void Executor::get_slot(int slot, int* variant, float* p0, float* p1, int* alias) {
@@ -1323,9 +1350,11 @@ void Executor::shutdown() {
   }
   cudaStreamSynchronize(s_own_);
   cudaStreamSynchronize(s_ctrl_);
+  if (states_) cudaFree(states_);
   if (ring_) cudaFree(ring_);
   if (dctrl_) cudaFree(dctrl_);
-  if (tab_dev_) cudaFree(tab_dev_);
+  for (cudaEvent_t& e : done_ev_)
+    if (e) cudaEventDestroy(e);
   if (partials_) cudaFree(partials_);
   if (counters_) cudaFree(counters_);
   if (arena_) cudaFreeHost(arena_);
@@ -1341,7 +1370,7 @@ void Executor::shutdown() {
   if (s_worker_) cudaStreamDestroy(s_worker_);
   if (s_ctrl_) cudaStreamDestroy(s_ctrl_);
   if (s_own_) cudaStreamDestroy(s_own_);
-  ring_ = nullptr; dctrl_ = nullptr; tab_dev_ = nullptr; partials_ = nullptr; counters_ = nullptr;
+  states_ = nullptr; ring_ = nullptr; dctrl_ = nullptr; partials_ = nullptr; counters_ = nullptr;
   arena_ = nullptr; hostblk_ = nullptr; last_event_ = nullptr;
   s_worker_ = s_ctrl_ = s_own_ = nullptr;
   if (!first_error.empty()) throw GError(GPUOS_EDEVICE, "shutdown: " + first_error);

@@ -137,7 +137,6 @@ class Executor {
   void ensure_worker_locked();
   void launch_worker_locked(uint64_t start);
   void ensure_scratch_locked();
-  void upload_tables_locked();
   bool wait_for_room_locked(std::unique_lock<std::mutex>& lk, uint64_t bytes, uint64_t floats,
                             uint64_t counters, uint64_t* arena_off, uint64_t* part_off,
                             uint64_t* cnt_off, uint64_t seq);
@@ -149,7 +148,6 @@ class Executor {
   int grid_ = 0;                // persistent worker grid (ingest CTA included)
   int batch_bps_ = 1;           // stream kernel: resident blocks per SM
   int total_warps_ = 1;         // warps that execute a batch (chunk sizing)
-  int unit_elems_ = 2048;       // elements per staged elementwise chunk
   uint64_t idle_ns_ = 0, wait_limit_ns_ = 0;
   double sync_timeout_s_ = 60.0;
 
@@ -168,8 +166,8 @@ class Executor {
 
   // device memory
   uint8_t* ring_ = nullptr;
+  BatchState* states_ = nullptr;   // device: per-batch counters, kDoneRing slots
   DevCtrl* dctrl_ = nullptr;
-  Tables* tab_dev_ = nullptr;
   float* partials_ = nullptr;
   uint64_t partials_cap_ = 0;
   uint32_t* counters_ = nullptr;
@@ -186,10 +184,13 @@ class Executor {
   uint32_t err_bits_ = 0;
   IntervalSet live_out_, live_in_;
   cudaStream_t last_stream_ = nullptr;
+  bool have_last_stream_ = false;
   cudaEvent_t last_event_ = nullptr;
   bool timing_ = false;
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed_;
   std::vector<cudaEvent_t> ev_pool_;
+  std::vector<cudaEvent_t> done_ev_ = std::vector<cudaEvent_t>(kDoneRing, nullptr);  // stream mode
+  std::string cuda_err_;        // first CUDA error a completion query reported
 
   Tables tab_;
   std::unordered_map<std::string, int> slot_of_key_;

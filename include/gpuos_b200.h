@@ -145,7 +145,8 @@ int32_t gpuos_submit_reduce(gpuos_executor* ex, int32_t slot, const gpuos_tensor
 int32_t gpuos_submit_task(gpuos_executor* ex, const void* task);
 
 /* Publish every queued request as one or more batches.  `stream` is the
- * cudaStream_t the inputs were produced on (NULL: the executor's stream).  In
+ * cudaStream_t the inputs were produced on (NULL: the legacy default stream,
+ * as everywhere in CUDA).  In
  * stream mode the batches run on that stream; in persistent mode the host
  * waits for that stream before ringing the doorbell.  With sync != 0 the call
  * returns after the batches are done (replaces flush(sync):
