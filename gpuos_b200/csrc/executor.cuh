@@ -209,12 +209,14 @@ __device__ __forceinline__ void ew_generic(const ReqView& q, const ExtRec* x, in
 // handles groups of 4 adjacent elements; vec_groups<V>() groups per lane are
 // loaded (128-bit for fp32, 64-bit for fp16/bf16) before any is computed or
 // stored, so that a warp keeps 32 x groups x 16 bytes per operand in flight:
-// 8 groups for the light operators, 4 for the transcendental ones (whose
-// temporaries need the registers).
+// 8 groups for the light operators (4 with per-row operands, whose offsets
+// take registers), 2 for the transcendental ones: their code is long, and a
+// batch that mixes operators runs many of them on one SM, so fewer unrolled
+// copies keep the instruction cache warm.
 // ---------------------------------------------------------------------------
 template <int V>
 __device__ __forceinline__ constexpr int vec_groups() {
-  return op_unroll<V>() == 2 ? 8 : 4;
+  return op_unroll<V>() == 2 ? 8 : 2;
 }
 
 enum OperandMode : int32_t { OM_LINEAR = 1, OM_ROW = 2, OM_ROWSPLAT = 3, OM_SCALAR = 4 };
@@ -289,6 +291,7 @@ __device__ __forceinline__ void ew_vec_flat(const VecView& u, float p0, float p1
   constexpr int kG = vec_groups<V>();
   const bool as = u.ma == OM_SCALAR, bs = u.mb == OM_SCALAR;
   int64_t i = 4 * (int64_t)lane;
+#pragma unroll 1
   for (; i + kStep * (kG - 1) + 4 <= n; i += kStep * kG) {
     float A[kG][4], B[kG][4];
 #pragma unroll
@@ -314,6 +317,7 @@ __device__ __forceinline__ void ew_vec_flat(const VecView& u, float p0, float p1
       st4(u.o, u.dto, e0 + i + kStep * g, R);
     }
   }
+#pragma unroll 1
   for (; i < n; i += kStep) {
     const int64_t e = e0 + i;
     if (i + 4 <= n) {
@@ -338,8 +342,9 @@ template <int V>
 __device__ __forceinline__ void ew_vec_rows(const VecView& u, float p0, float p1, int64_t e0,
                                             int64_t n, int lane) {
   constexpr int64_t kStep = 4 * 32;
-  constexpr int kG = 4;
+  constexpr int kG = op_unroll<V>() == 2 ? 4 : 2;
   int64_t i = 4 * (int64_t)lane;
+#pragma unroll 1
   for (; i + kStep * (kG - 1) + 4 <= n; i += kStep * kG) {
     float A[kG][4], B[kG][4];
     int64_t oo[kG];
@@ -358,6 +363,7 @@ __device__ __forceinline__ void ew_vec_rows(const VecView& u, float p0, float p1
       st4(u.o, u.dto, oo[g], R);
     }
   }
+#pragma unroll 1
   for (; i < n; i += kStep) {
     const int64_t e = e0 + i;
     if (i + 4 <= n) {
