@@ -415,6 +415,30 @@ def bench_reference(args, world, rank):
     }
 
 
+def profile_case(dev="cuda:0"):
+    """The small case the committed ncu captures use: two stream-mode launches
+    of gpuos_batch_kernel (one executor, batches of up to 2048 requests):
+    2048 fp32 adds of 8192 elements (201 MB), then the first 2048 requests of
+    the mixed 24-operator stream.  A few GB on the device at most."""
+    import gpuos_b200.cabi as C
+    from gpuos_b200 import workloads as W
+    with C.Executor(0, mode=C.MODE_STREAM, max_batch=2048) as e:
+        A = torch.randn(2048, 8192, device=dev)
+        B = torch.randn(2048, 8192, device=dev)
+        O = torch.empty(2048, 8192, device=dev)
+        for i in range(2048):
+            e.builtin(C.OP_ADD, A[i], B[i], O[i])
+        e.flush(sync=True)
+        st = W.mixed_24op(n_req=2048, seed=0)
+        din, dout = st.device_buffers(dev)
+        calls = W.Submitter(_CabiExt(e)).prepare(st, st.views(din, dout))
+        for fn, a in calls:
+            fn(*a)
+        e.flush(sync=True)
+        assert torch.equal(O, A + B)
+    print("profile case done", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -424,7 +448,12 @@ def main():
     ap.add_argument("--mode", default=os.environ.get("GPUOS_MODE", "persistent"),
                     choices=["persistent", "stream"])
     ap.add_argument("--workload", default="mixed_24op")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="run the small two-launch case of the committed ncu captures and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case()
+        return
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = (1, 0, 0) if args.impl == "reference" and "WORLD_SIZE" not in os.environ \

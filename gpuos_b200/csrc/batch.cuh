@@ -53,8 +53,10 @@ struct Cur {
 // The record carries the operator the request's slot named when it was
 // flushed (the host resolves the jump table), and its parameters.  A strided
 // request's ExtRec is copied from the arena to the warp's shared-memory slot.
-__device__ __forceinline__ void decode(Cur& cur, const Exec& ex, const Req* rec, ExtRec* xs) {
-  const ReqView q = load_req(rec, ex.lane);
+// `words`: the record as load_req_words returned it (loaded ahead of time).
+__device__ __forceinline__ void decode(Cur& cur, const Exec& ex, const Req* rec, uint4 words,
+                                       ExtRec* xs) {
+  const ReqView q = decode_req(words);
   cur.rec = rec;
   cur.v = q.op == kOpNone ? V_NONE : q.op;
   cur.p0 = q.p0;
@@ -103,16 +105,32 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
   int r = -1;
   uint32_t rbase = 0, rend = 0;
   Cur cur;
+  // granule j's entry, its first request's record words and end, loaded ahead
+  uint2 g = make_uint2(0u, 0u);
+  uint4 gw_rec = make_uint4(0u, 0u, 0u, 0u);
+  uint32_t g_end = 0;
+  if (j < ngran) {
+    g = __ldcg(ex.gtab + j);
+    gw_rec = load_req_words(ex.recs + g.x, lane);
+    g_end = __ldcg(ex.gcb + g.x + 1);
+  }
   while (j < ngran) {
     const uint32_t jn = staged ? claim() : j + W;  // the next granule, known ahead
+    const uint2 gn = jn < ngran ? __ldcg(ex.gtab + jn) : make_uint2(0u, 0u);
     uint32_t c = j * G;
     const uint32_t cend = min(c + G, nchunk);
-    const uint2 g = __ldcg(ex.gtab + j);
     if ((int)g.x != r) {
       r = (int)g.x;
       rbase = g.y;
-      rend = __ldcg(ex.gcb + r + 1);
-      decode(cur, ex, ex.recs + r, xs);
+      rend = g_end;
+      decode(cur, ex, ex.recs + r, gw_rec, xs);
+    }
+    // the next granule's record is in flight while this one runs
+    uint4 n_rec = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t n_end = 0;
+    if (jn < ngran) {
+      n_rec = load_req_words(ex.recs + gn.x, lane);
+      n_end = __ldcg(ex.gcb + gn.x + 1);
     }
     for (; c < cend; ++c) {
       if (c >= rend) {
@@ -121,7 +139,7 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
           rbase = rend;
           rend = __ldcg(ex.gcb + r + 1);
         } while (c >= rend);
-        decode(cur, ex, ex.recs + r, xs);
+        decode(cur, ex, ex.recs + r, load_req_words(ex.recs + r, lane), xs);
       }
       if (staged) {
         const uint32_t w = __ldcg(ex.req_wait + r);
@@ -154,6 +172,9 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
       }
     }
     j = jn;
+    g = gn;
+    gw_rec = n_rec;
+    g_end = n_end;
   }
   return count;
 }

@@ -89,9 +89,14 @@ __device__ __forceinline__ uint64_t u64of(uint32_t lo, uint32_t hi) {
 // Decode the 128-byte record (whole warp): lanes 0..7 read it as one
 // coalesced 128-byte load through L2 (the staging ring is rewritten for later
 // batches, so never from L1), and shuffles hand the words to every lane.
-__device__ __forceinline__ ReqView load_req(const Req* g, int lane) {
+__device__ __forceinline__ uint4 load_req_words(const Req* g, int lane) {
   uint4 w = make_uint4(0u, 0u, 0u, 0u);
   if (lane < 8) w = __ldcg(reinterpret_cast<const uint4*>(g) + lane);
+  return w;
+}
+
+// The record from the words lanes 0..7 hold (load_req_words).
+__device__ __forceinline__ ReqView decode_req(uint4 w) {
   auto word = [&](int i) {
     uint4 r;
     r.x = __shfl_sync(GPUOS_FULL, w.x, i);
@@ -131,6 +136,10 @@ __device__ __forceinline__ ReqView load_req(const Req* g, int lane) {
   q.fdiv_s = w7.z;
   q.rg = w7.w;
   return q;
+}
+
+__device__ __forceinline__ ReqView load_req(const Req* g, int lane) {
+  return decode_req(load_req_words(g, lane));
 }
 
 __device__ __forceinline__ int64_t row_of(const ReqView& q, int64_t e) {
