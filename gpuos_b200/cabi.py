@@ -80,6 +80,7 @@ SIGNATURES = {
                                                 P(Tensor), P(Tensor), P(Tensor), P(Plan)]),
     "gpuos_plan_reduce": (ctypes.c_int32, [ctypes.c_int32, P(Tensor), P(Tensor), P(ctypes.c_int32),
                                            ctypes.c_int32, ctypes.c_int32, P(Plan)]),
+    "gpuos_jit_check": (ctypes.c_int32, [ctypes.c_char_p, ctypes.c_int32]),
     "gpuos_reduce_rows_noalloc": (ctypes.c_int32, [ctypes.c_int32, _VP, ctypes.c_int32,
                                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                                    _VP, ctypes.c_int32, _VP]),
@@ -246,6 +247,14 @@ class Executor:
 
     def set_slot(self, slot, variant, p0=0.0, p1=0.0):
         check(lib().gpuos_set_slot(self.h, slot, variant, p0, p1))
+
+    def get_slot(self, slot):
+        """(variant, p0, p1, alias) of a slot."""
+        v, a = ctypes.c_int32(), ctypes.c_int32()
+        p0, p1 = ctypes.c_float(), ctypes.c_float()
+        check(lib().gpuos_get_slot(self.h, slot, ctypes.byref(v), ctypes.byref(p0),
+                                   ctypes.byref(p1), ctypes.byref(a)))
+        return v.value, p0.value, p1.value, a.value
 
     def set_timing(self, on: bool):
         check(lib().gpuos_set_timing(self.h, int(bool(on))))

@@ -24,15 +24,13 @@ namespace gpuos {
 
 #define GPUOS_FULL 0xffffffffu
 
-#ifndef GPUOS_JIT_KNOWN
-#define GPUOS_JIT_KNOWN(v) false
-#endif
-#ifndef GPUOS_JIT_VEC_CASES
-#define GPUOS_JIT_VEC_CASES
-#endif
-
+// The elementwise variants this kernel can run (GPUOS_ALL_EW).
 __device__ __forceinline__ bool ew_known(int v) {
-  return (v >= 0 && v < V_NUM_EW) || GPUOS_JIT_KNOWN(v);
+#ifdef GPUOS_JIT_LINK
+  return v >= V_JIT_BASE && v < V_JIT_BASE + kJitOps;
+#else
+  return v >= 0 && v < V_NUM_EW;
+#endif
 }
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -408,7 +406,6 @@ __device__ __forceinline__ bool ew_vec_dispatch(int v, const VecView& u, float p
                                                 int64_t e0, int64_t n, int lane) {
   switch (v) {
     GPUOS_ALL_EW(GPUOS_VEC_CASE)
-    GPUOS_JIT_VEC_CASES
     default: return false;
   }
 }
@@ -626,6 +623,10 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
     ew_generic(q, x, v, p0, p1, e0, e1, ex.lane);
     return;
   }
+#ifdef GPUOS_JIT_LINK
+  // the kernel for custom expressions runs elementwise batches only
+  if (ex.lane == 0) set_err(ex, ERR_BAD_KIND);
+#else
   if (v != V_SUM && v != V_MEAN) {
     if (ex.lane == 0) set_err(ex, v < 0 ? ERR_BAD_OP : ERR_BAD_KIND);
     return;
@@ -634,6 +635,7 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
   if (q.layout == RL_ROWS) red_rows(ex, q, mean, k);
   else if (q.layout == RL_COLS) red_cols(ex, q, mean, k);
   else red_generic(ex, q, x, mean, k);
+#endif
 }
 
 // Called by the thread that counted the last chunk of the batch.  The

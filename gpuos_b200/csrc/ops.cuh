@@ -17,8 +17,38 @@
 
 namespace gpuos {
 
+// Custom expressions (variants V_JIT_BASE + k): in the relocatable batch
+// kernel for custom expressions (GPUOS_JIT_LINK) these are external device
+// functions, compiled from the expression strings by NVRTC and linked in at
+// run time.
+static constexpr int kJitOps = 16;
+#ifdef GPUOS_JIT_LINK
+extern "C" {
+#define GPUOS_JIT_DECL(k) __device__ float gpuos_jit_op##k(float A, float B, float p0, float p1);
+GPUOS_JIT_DECL(0) GPUOS_JIT_DECL(1) GPUOS_JIT_DECL(2) GPUOS_JIT_DECL(3)
+GPUOS_JIT_DECL(4) GPUOS_JIT_DECL(5) GPUOS_JIT_DECL(6) GPUOS_JIT_DECL(7)
+GPUOS_JIT_DECL(8) GPUOS_JIT_DECL(9) GPUOS_JIT_DECL(10) GPUOS_JIT_DECL(11)
+GPUOS_JIT_DECL(12) GPUOS_JIT_DECL(13) GPUOS_JIT_DECL(14) GPUOS_JIT_DECL(15)
+#undef GPUOS_JIT_DECL
+}
+template <int K>
+__device__ __forceinline__ float jit_op(float A, float B, float p0, float p1) {
+#define GPUOS_JIT_CALL(k) if constexpr (K == k) return gpuos_jit_op##k(A, B, p0, p1);
+  GPUOS_JIT_CALL(0) GPUOS_JIT_CALL(1) GPUOS_JIT_CALL(2) GPUOS_JIT_CALL(3)
+  GPUOS_JIT_CALL(4) GPUOS_JIT_CALL(5) GPUOS_JIT_CALL(6) GPUOS_JIT_CALL(7)
+  GPUOS_JIT_CALL(8) GPUOS_JIT_CALL(9) GPUOS_JIT_CALL(10) GPUOS_JIT_CALL(11)
+  GPUOS_JIT_CALL(12) GPUOS_JIT_CALL(13) GPUOS_JIT_CALL(14) GPUOS_JIT_CALL(15)
+#undef GPUOS_JIT_CALL
+  return A;
+}
+#endif
+
 template <int V>
 __device__ __forceinline__ float op1(float A, float B, float p0, float p1) {
+#ifdef GPUOS_JIT_LINK
+  if constexpr (V >= V_JIT_BASE && V < V_JIT_BASE + kJitOps) return jit_op<V - V_JIT_BASE>(A, B, p0, p1);
+  else
+#endif
   if constexpr (V == V_ADD) return A + B;
   else if constexpr (V == V_MUL) return A * B;
   else if constexpr (V == V_SUB) return A - B;
@@ -49,22 +79,26 @@ __device__ __forceinline__ float op1(float A, float B, float p0, float p1) {
   else return A;  // V_COPY
 }
 
-// Custom (NVRTC) expressions are spliced in here by the JIT executor source.
-#ifndef GPUOS_JIT_CASES1
-#define GPUOS_JIT_CASES1
-#endif
-
 #define GPUOS_CASE1(V) case V: r = op1<V>(A, B, p0, p1); return true;
+// The elementwise variants a kernel instantiates: the precompiled operators,
+// or (in the kernel for custom expressions) the custom slots.
+#ifdef GPUOS_JIT_LINK
+#define GPUOS_ALL_EW(M) \
+  M(V_JIT_BASE + 0) M(V_JIT_BASE + 1) M(V_JIT_BASE + 2) M(V_JIT_BASE + 3) \
+  M(V_JIT_BASE + 4) M(V_JIT_BASE + 5) M(V_JIT_BASE + 6) M(V_JIT_BASE + 7) \
+  M(V_JIT_BASE + 8) M(V_JIT_BASE + 9) M(V_JIT_BASE + 10) M(V_JIT_BASE + 11) \
+  M(V_JIT_BASE + 12) M(V_JIT_BASE + 13) M(V_JIT_BASE + 14) M(V_JIT_BASE + 15)
+#else
 #define GPUOS_ALL_EW(M) \
   M(V_ADD) M(V_MUL) M(V_SUB) M(V_DIV0) M(V_DIV) M(V_MAX) M(V_MIN) M(V_POW) \
   M(V_RELU) M(V_SIGMOID) M(V_TANH) M(V_EXP) M(V_LOG) M(V_SQRT) M(V_ABS) \
   M(V_HARDSIGMOID) M(V_HARDSWISH) M(V_GELU) M(V_SIN) M(V_COS) M(V_LEAKY_RELU) \
   M(V_CLAMP) M(V_ELU) M(V_SOFTPLUS) M(V_CLAMP_MIN) M(V_CLAMP_MAX) M(V_COPY)
+#endif
 
 __device__ __forceinline__ bool ew_apply1(int v, float A, float B, float& r, float p0, float p1) {
   switch (v) {
     GPUOS_ALL_EW(GPUOS_CASE1)
-    GPUOS_JIT_CASES1
     default: return false;
   }
 }
@@ -77,7 +111,7 @@ __device__ __forceinline__ bool ew_apply1(int v, float A, float B, float& r, flo
 // warm and the register budget low).
 template <int V>
 __device__ __forceinline__ constexpr int op_unroll() {
-  return (V == V_POW || V == V_SIGMOID || V == V_TANH || V == V_EXP || V == V_LOG ||
+  return (V >= V_JIT_BASE || V == V_POW || V == V_SIGMOID || V == V_TANH || V == V_EXP || V == V_LOG ||
           V == V_GELU || V == V_SIN || V == V_COS || V == V_ELU || V == V_SOFTPLUS ||
           V == V_DIV || V == V_DIV0 || V == V_SQRT || V == V_HARDSWISH)
              ? 1

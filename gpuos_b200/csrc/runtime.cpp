@@ -998,6 +998,15 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     uint32_t* w = reinterpret_cast<uint32_t*>(base + wait_off);
     for (uint32_t r = 0; r < n; ++r) w[r] = stage_first[r] ? cb[stage_first[r]] : 0u;
   }
+  const bool jit_batch = var[0] >= V_JIT_BASE;  // a batch is all custom or all precompiled
+  if (jit_batch && opt_.mode == GPUOS_MODE_PERSISTENT) {
+    // Custom expressions do not run in the resident worker: the batch runs
+    // after every earlier batch, on its own launch, before any later one.  It
+    // takes no sequence number; its staging memory is freed with the next
+    // batch's.
+    run_jit_batch_sync_locked(lk, aoff, bytes, ngran, h);
+    return;
+  }
   next_seq_ = seq + 1;
 
   if (opt_.mode == GPUOS_MODE_PERSISTENT) {
@@ -1037,8 +1046,13 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       }
       GCU(cudaEventRecord(e0, stream));
     }
-    GCU(gpuos_launch_batch(ring_ + aoff, h, states_ + seq % kDoneRing, dr, wait_limit_ns_, grid,
-                           stream));
+    if (jit_batch) {
+      jit_launch(jit_kernels_.back(), grid, block_, stream, ring_ + aoff, *h,
+                 states_ + seq % kDoneRing, dr, wait_limit_ns_);
+    } else {
+      GCU(gpuos_launch_batch(ring_ + aoff, h, states_ + seq % kDoneRing, dr, wait_limit_ns_, grid,
+                             stream));
+    }
     if (timing_) {
       GCU(cudaEventRecord(e1, stream));
       timed_.emplace_back(e0, e1);
@@ -1049,6 +1063,78 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     GCU(cudaEventRecord(de, stream));
     last_stream_ = stream;
     have_last_stream_ = true;
+  }
+}
+
+// The variant a request's record will carry (its slot resolved now).
+int Executor::variant_of(const Pending& p) const {
+  if (!(p.r.flags & RF_SLOT)) return p.r.op;
+  const int s = p.r.op;
+  const int phys = (s >= 0 && s < kMaxSlots) ? tab_.alias[s] : -1;
+  return (phys >= 0 && phys < kMaxSlots) ? tab_.slot[phys].variant : V_NONE;
+}
+
+// Persistent mode: one batch of custom-expression requests, staged at `aoff`
+// of the arena, run on the executor's stream once every earlier batch is done.
+void Executor::run_jit_batch_sync_locked(std::unique_lock<std::mutex>& lk, uint64_t aoff,
+                                         uint64_t bytes, uint64_t ngran, BatchHdr* h) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int it = 0;; ++it) {
+    reclaim();
+    if (done_wm_ == next_seq_) break;
+    ensure_worker_locked();
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() >
+        sync_timeout_s_)
+      throw GError(GPUOS_ETIMEOUT, "timed out waiting for earlier batches");
+    lk.unlock();
+    if (it < 64) GPUOS_PAUSE();
+    else std::this_thread::sleep_for(std::chrono::microseconds(20));
+    lk.lock();
+  }
+  DeviceGuard g(device_);
+  if (worker_launched_) {
+    // the resident worker holds the SMs' registers: let it exit first (it is
+    // idle); the next batch relaunches it
+    hctrl_->quit = 1u;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    const auto t1 = std::chrono::steady_clock::now();
+    cudaError_t q;
+    while ((q = cudaStreamQuery(s_worker_)) == cudaErrorNotReady) {
+      if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t1).count() >
+          sync_timeout_s_)
+        throw GError(GPUOS_ETIMEOUT, "persistent worker did not exit");
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    hctrl_->quit = 0u;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    worker_launched_ = false;
+    if (q != cudaSuccess) GCU(q);
+  }
+  if (!jit_state_) {
+    GCU(cudaMalloc(reinterpret_cast<void**>(&jit_state_), sizeof(BatchState)));
+    GCU(cudaMemset(jit_state_, 0, sizeof(BatchState)));
+    void* w = nullptr;
+    GCU(cudaHostAlloc(&w, 64, cudaHostAllocMapped));
+    jit_word_ = static_cast<volatile uint64_t*>(w);
+  }
+  h->seq = 0;  // its error word is jit_word_[0]
+  jit_word_[0] = 0;
+  void* wd = nullptr;
+  GCU(cudaHostGetDevicePointer(&wd, const_cast<uint64_t*>(jit_word_), 0));
+  GCU(cudaMemcpyAsync(ring_ + aoff, arena_ + aoff, bytes, cudaMemcpyHostToDevice, s_own_));
+  const uint64_t wpc = (uint64_t)block_ / 32;
+  int grid = (int)std::min<uint64_t>((uint64_t)sm_count_ * batch_bps_, (ngran + wpc - 1) / wpc);
+  jit_launch(jit_kernels_.back(), std::max(grid, 1), block_, s_own_, ring_ + aoff, *h,
+             jit_state_, static_cast<volatile uint64_t*>(wd), wait_limit_ns_);
+  GCU(cudaStreamSynchronize(s_own_));
+  const uint64_t w = jit_word_[0];
+  if ((w & kDoneMask) == 1) {
+    const uint32_t e = (uint32_t)((w >> 48) & 0xffu);
+    if (e) {
+      ++errors_;
+      throw GError(GPUOS_EDEVICE, "gpuos batch error in a custom-expression batch (bits " +
+                                      std::to_string(e) + ")");
+    }
   }
 }
 
@@ -1074,8 +1160,10 @@ uint64_t Executor::flush(bool sync, cudaStream_t stream) {
       while (i < reqs.size()) {
         size_t j = i;
         uint64_t bytes = 256, floats = 0, cnts = 0, chunks = 0;
+        const bool jit = variant_of(reqs[i]) >= V_JIT_BASE;
         while (j < reqs.size() && j - i < (size_t)opt_.max_batch) {
           const Pending& p = reqs[j];
+          if (j > i && (variant_of(p) >= V_JIT_BASE) != jit) break;
           const uint64_t b = 136 + (p.has_ext ? sizeof(ExtRec) : 0);
           if (j > i && (bytes + b > budget || floats + p.partials > (16ull << 20) / 2 ||
                         cnts + p.counters > (4ull << 20) / 2 ||
@@ -1207,12 +1295,19 @@ int Executor::register_elementwise(const std::string& key, const std::string& ex
   if (it != slot_of_key_.end()) return it->second;
   if (arity != 1 && arity != 2) throw GError(GPUOS_EINVAL, "arity must be 1 or 2");
   float p0 = 0.f, p1 = 0.f;
-  const int v = match_builtin_expr(expr, arity, &p0, &p1);
-  if (v < 0)
-    throw GError(GPUOS_EUNSUPPORTED,
-                 "expression is not one of the precompiled operators and the NVRTC path is "
-                 "not available: " + expr);
+  int v = match_builtin_expr(expr, arity, &p0, &p1);
   if (next_slot_ >= kMaxSlots) throw GError(GPUOS_EINVAL, "jump table is full (128 slots)");
+  if (v < 0) {
+    // not a precompiled operator: compile it (with the earlier custom ones)
+    // and link a new batch kernel
+    std::vector<std::string> exprs = jit_exprs_;
+    exprs.push_back(expr);
+    const std::vector<char> cubin = jit_compile(exprs);
+    DeviceGuard g(device_);
+    jit_kernels_.push_back(jit_link(cubin));
+    jit_exprs_ = exprs;
+    v = V_JIT_BASE + (int)jit_exprs_.size() - 1;
+  }
   const int slot = next_slot_++;
   tab_.slot[slot] = SlotEntry{v, p0, p1, arity};
   slot_of_key_.emplace(key, slot);
@@ -1244,6 +1339,7 @@ void Executor::set_alias(int logical, int physical) {
 void Executor::set_slot(int slot, int variant, float p0, float p1) {
   if (slot < 0 || slot >= kMaxSlots) throw GError(GPUOS_EINVAL, "slot out of range");
   const bool ok = variant == V_NONE || (variant >= 0 && variant < V_NUM_EW) ||
+                  (variant >= V_JIT_BASE && variant < V_JIT_BASE + (int)jit_exprs_.size()) ||
                   variant == V_SUM || variant == V_MEAN;
   if (!ok) throw GError(GPUOS_EINVAL, "unknown operator id " + std::to_string(variant));
   std::lock_guard<std::mutex> lk(mu_);
@@ -1351,6 +1447,12 @@ void Executor::shutdown() {
   cudaStreamSynchronize(s_own_);
   cudaStreamSynchronize(s_ctrl_);
   if (states_) cudaFree(states_);
+  for (JitKernel& k : jit_kernels_) jit_unload(k);
+  jit_kernels_.clear();
+  if (jit_state_) cudaFree(jit_state_);
+  if (jit_word_) cudaFreeHost(const_cast<uint64_t*>(jit_word_));
+  jit_state_ = nullptr;
+  jit_word_ = nullptr;
   if (ring_) cudaFree(ring_);
   if (dctrl_) cudaFree(dctrl_);
   for (cudaEvent_t& e : done_ev_)

@@ -27,6 +27,7 @@
 
 #include "../../include/gpuos_b200.h"
 #include "gpuos_abi.h"
+#include "jit.h"
 
 namespace gpuos {
 
@@ -194,6 +195,14 @@ class Executor {
 
   Tables tab_;
   std::unordered_map<std::string, int> slot_of_key_;
+  // custom expressions (variants V_JIT_BASE + k) and the batch kernel linked with them
+  std::vector<std::string> jit_exprs_;
+  std::vector<JitKernel> jit_kernels_;  // every one linked so far (in-flight batches may use any)
+  BatchState* jit_state_ = nullptr;     // persistent mode: counters of custom-expression batches
+  volatile uint64_t* jit_word_ = nullptr;  // persistent mode: their error word (mapped)
+  int variant_of(const Pending& p) const;
+  void run_jit_batch_sync_locked(std::unique_lock<std::mutex>& lk, uint64_t aoff, uint64_t bytes,
+                                 uint64_t ngran, BatchHdr* h);
   int next_slot_ = 20;       // slots below 20 are reserved as in the reference (gpuos_ext.cpp:95)
 
   bool started_ = false;

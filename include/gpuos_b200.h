@@ -114,8 +114,8 @@ int32_t gpuos_submit_builtin(gpuos_executor* ex, int32_t op, const gpuos_tensor*
                              const gpuos_tensor* b, const gpuos_tensor* out);
 
 /* Queue a request through jump-table slot `slot` (replaces submit_unary /
- * submit_binary: gpuos_ext.cpp:695-707).  The slot is resolved on the device
- * when the batch runs, so a hot swap affects every batch that starts after it. */
+ * submit_binary: gpuos_ext.cpp:695-707).  The slot is resolved when the
+ * request is flushed, so a hot swap affects every request flushed after it. */
 int32_t gpuos_submit_unary(gpuos_executor* ex, int32_t slot, const gpuos_tensor* a,
                            const gpuos_tensor* out);
 int32_t gpuos_submit_binary(gpuos_executor* ex, int32_t slot, const gpuos_tensor* a,
@@ -203,6 +203,12 @@ int32_t gpuos_plan_elementwise(int32_t variant, float p0, float p1, const gpuos_
                                const gpuos_tensor* b, const gpuos_tensor* out, gpuos_plan* plan);
 int32_t gpuos_plan_reduce(int32_t variant, const gpuos_tensor* x, const gpuos_tensor* out,
                           const int32_t* axes, int32_t naxes, int32_t keepdim, gpuos_plan* plan);
+
+/* Compile a custom expression with NVRTC only, to check it (no GPU needed):
+ * GPUOS_OK, GPUOS_ENVRTC with the compiler log in gpuos_last_error(), or
+ * GPUOS_EUNSUPPORTED when NVRTC is not installed (replaces the compile step of
+ * ensure_elementwise_registered: gpuos_ext.cpp:625-692). */
+int32_t gpuos_jit_check(const char* expr, int32_t arity);
 
 /* Which precompiled operator (and parameters) an expression string of the
  * reference scheduler maps to; *variant = -1 when it needs NVRTC. */

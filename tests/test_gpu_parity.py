@@ -558,3 +558,89 @@ def test_stream_mode_orders_with_torch():
         assert torch.equal(d, (a + a * 3) * 2)
     finally:
         g.shutdown()
+
+
+# ---------------------------------------------------------------------------
+# Custom expressions (NVRTC): compiled at registration, linked to the batch
+# kernel for custom expressions, batched like every other request.
+# ---------------------------------------------------------------------------
+def _f32_ref(fn, *xs):
+    """fn evaluated in float64 on float32 inputs: the exact value the fp32
+    result approximates."""
+    return fn(*[np.asarray(x, np.float64) for x in xs])
+
+
+@pytest.mark.parametrize("mode", MODES, ids=MODE_IDS)
+def test_custom_expressions(mode):
+    with C.Executor(0, mode=mode) as e:
+        s2 = e.register_elementwise("cx|quad", "A * A + 2.f * B", 2)
+        s1 = e.register_elementwise("cx|wave", "sinf(A) * 0.5f + expf(-A)", 1)
+        assert e.register_elementwise("cx|quad", "A * A + 2.f * B", 2) == s2
+        g = torch.Generator().manual_seed(77)
+        keep = []
+        for n, dt in ((1, torch.float32), (4099, torch.float32), (3000, torch.float16),
+                      (2048, torch.bfloat16)):
+            a = torch.randn(n, generator=g).to(dt)
+            b = torch.randn(n, generator=g).to(dt)
+            ga, gb = gpu(a), gpu(b)
+            o2 = torch.empty(n, device=DEV)
+            o1 = torch.empty(n, device=DEV, dtype=dt)
+            e.binary(s2, ga, gb, o2)
+            e.unary(s1, ga, o1)
+            keep.append((a, b, ga, gb, o2, o1))
+        # a strided (transposed) operand takes the general path
+        x = torch.randn(33, 70, generator=g)
+        gx = gpu(x).t()
+        ox = torch.empty(70, 33, device=DEV)
+        e.unary(s1, gx, ox)
+        e.flush(sync=True)
+        for a, b, ga, gb, o2, o1 in keep:
+            A, B = a.float().numpy(), b.float().numpy()
+            want2 = _f32_ref(lambda p, q: p * p + 2.0 * q, A, B)
+            got2 = o2.cpu().double().numpy()
+            tol2 = (np.abs(A.astype(np.float64)) ** 2 + 2 * np.abs(B)) * 2.0 ** -22
+            assert np.all(np.abs(got2 - want2) <= tol2 + 1e-30)
+            want1 = _f32_ref(lambda p: np.sin(p) * 0.5 + np.exp(-p), A)
+            got1 = o1.cpu().double().numpy()
+            ulp_out = 2.0 ** -22 if o1.dtype == torch.float32 else (
+                2.0 ** -10 if o1.dtype == torch.float16 else 2.0 ** -7)
+            tol1 = (0.5 * np.abs(np.sin(A)) + np.exp(-A.astype(np.float64))) * (2.0 ** -20 + ulp_out)
+            assert np.all(np.abs(got1 - want1) <= tol1 + 1e-30)
+        wantx = _f32_ref(lambda p: np.sin(p) * 0.5 + np.exp(-p), x.t().numpy())
+        tolx = (0.5 * np.abs(np.sin(x.t().numpy())) + np.exp(-x.t().double().numpy())) * 2.0 ** -20
+        assert np.all(np.abs(ox.cpu().double().numpy() - wantx) <= tolx)
+
+
+@pytest.mark.parametrize("mode", MODES, ids=MODE_IDS)
+def test_custom_expression_ordering_and_hot_swap(mode):
+    """A custom request that reads a precompiled request's output in the same
+    flush runs after it (the flush splits into batches in order); a slot can
+    be swapped onto a custom expression."""
+    with C.Executor(0, mode=mode) as e:
+        sc = e.register_elementwise("cx|cube", "A * A * A", 1)
+        g = torch.Generator().manual_seed(78)
+        a, b = torch.randn(5000, generator=g), torch.randn(5000, generator=g)
+        ga, gb = gpu(a), gpu(b)
+        t = torch.empty(5000, device=DEV)
+        y = torch.empty(5000, device=DEV)
+        z = torch.empty(5000, device=DEV)
+        e.builtin(C.OP_ADD, ga, gb, t)       # precompiled
+        e.unary(sc, t, y)                    # custom, reads t
+        e.builtin(C.OP_MUL, y, gb, z)        # precompiled, reads y
+        e.flush(sync=True)
+        T = (a + b).numpy().astype(np.float64)
+        assert np.allclose(y.cpu().double().numpy(), T ** 3, rtol=1e-6, atol=1e-6)
+        assert torch.equal(z.cpu(), y.cpu() * b)
+        # hot swap: slot 0 (add) onto the custom cube, then back
+        v, _, _, _ = e.get_slot(sc)
+        assert v >= 64
+        e.set_slot(0, v)
+        w = torch.empty(5000, device=DEV)
+        e.binary(0, ga, gb, w)
+        e.flush(sync=True)
+        assert np.allclose(w.cpu().double().numpy(), a.double().numpy() ** 3, rtol=1e-6,
+                           atol=1e-6)
+        e.set_slot(0, C.variant("add"))
+        e.binary(0, ga, gb, w)
+        e.flush(sync=True)
+        assert torch.equal(w.cpu(), a + b)

@@ -217,3 +217,14 @@ def test_workload_shapes():
     c1 = W.micro_add_mul(n_req=8)
     assert [r.op for r in c1.requests] == ["add", "mul"] * 4
     assert c1.algo_bytes == 8 * 4096 * 12
+
+
+def test_custom_expression_compile_check():
+    """NVRTC compiles custom expressions on the host (no GPU needed)."""
+    L = C.lib()
+    assert L.gpuos_jit_check(b"A * A + 2.f * B", 2) == C.OK
+    assert L.gpuos_jit_check(b"sinf(A) * 0.5f + expf(-A)", 1) == C.OK
+    assert L.gpuos_jit_check(b"A +* B", 2) == C.ENVRTC
+    assert "nvrtc" in L.gpuos_last_error().decode()
+    assert L.gpuos_jit_check(b"A; }", 1) == C.EINVAL
+    assert L.gpuos_jit_check(b"A // c", 1) == C.EINVAL
