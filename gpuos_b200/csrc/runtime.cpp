@@ -681,13 +681,18 @@ void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
 
 void Executor::submit_ew(int op, bool is_slot, float p0, float p1, const gpuos_tensor* a,
                          const gpuos_tensor* b, const gpuos_tensor& out) {
-  Pending p;
-  build_ew(p, op, is_slot, p0, p1, a, b, out);
   std::lock_guard<std::mutex> lk(mu_);
   if (!started_) throw GError(GPUOS_ESTATE, "executor is shut down");
+  // planned in place: a Pending is large (it can hold a strided layout)
+  pending_.emplace_back();
+  try {
+    build_ew(pending_.back(), op, is_slot, p0, p1, a, b, out);
+  } catch (...) {
+    pending_.pop_back();
+    throw;
+  }
   ++requests_;
-  if (p.nchunk == 0) return;  // empty output: nothing to do
-  pending_.push_back(p);
+  if (pending_.back().nchunk == 0) pending_.pop_back();  // empty output: nothing to do
 }
 
 void Executor::submit_reduce(int op, bool is_slot, const gpuos_tensor& x,

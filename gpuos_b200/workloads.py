@@ -147,6 +147,31 @@ class Stream:
     def algo_bytes(self) -> int:
         return sum(r.algo_bytes for r in self.requests)
 
+    def batch_spans(self):
+        """Per flush group of `flush_every` requests: the byte ranges
+        (in_lo, in_hi, out_lo, out_hi) of the two slabs its tensors cover.
+        Slabs are allocated in request order, so the groups' ranges follow
+        one another."""
+        def span(t: TensorSpec):
+            n = 1
+            for sz, st in zip(t.shape, t.strides):
+                n += (sz - 1) * st if sz > 0 else 0
+            return t.off, t.off + n * _ESZ[t.dtype]
+        res = []
+        fe = self.flush_every
+        for i in range(0, len(self.requests), fe):
+            ilo = olo = 1 << 62
+            ihi = ohi = 0
+            for r in self.requests[i:i + fe]:
+                for t in (r.a, r.b):
+                    if t is not None:
+                        lo, hi = span(t)
+                        ilo, ihi = min(ilo, lo), max(ihi, hi)
+                lo, hi = span(r.out)
+                olo, ohi = min(olo, lo), max(ohi, hi)
+            res.append((ilo, ihi, olo, ohi))
+        return res
+
     def device_buffers(self, device, pin=False):
         """(inputs, outputs) byte slabs on `device` with the inputs copied."""
         din = self.host_in.to(device)
