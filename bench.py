@@ -118,7 +118,7 @@ def dist_setup(n_gpus):
 
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
@@ -126,12 +126,20 @@ def dist_setup(n_gpus):
 
 
 def allmax(x: float, world: int) -> float:
+    """The max of x over the ranks (NCCL on the GPUs, gloo on the CPU)."""
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def whole_job_rate(units_per_rank: int, seconds: float, world: int) -> float:
+    """Units all ranks processed / the slowest rank's time (weak scaling:
+    every rank runs the same amount of work)."""
+    return world * units_per_rank / allmax(seconds, world)
 
 
 def barrier(world):
@@ -369,7 +377,7 @@ def bench_ours(args, world, rank, local):
     wall = time.perf_counter() - t0
     q1 = ext.peek_queue()
     ev_s = ev0.elapsed_time(ev1) / 1e3
-    t_step = allmax(max(ev_s, wall) / args.steps, world)
+    t_step = allmax(max(ev_s, wall) / args.steps, world)  # per step, slowest rank
     torch.cuda.synchronize()
     clk = clocks.stop()
     batches = q1["tail"] - q0["tail"]
