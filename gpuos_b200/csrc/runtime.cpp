@@ -838,24 +838,56 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   // hazards between the requests of this batch: a request that reads what an
   // earlier request of its stage writes (or writes what it reads or writes)
   // opens a new stage; chunks of a stage start after the previous stage is done.
-  std::vector<uint32_t> stage_first(n);
+  std::vector<uint32_t> stage_first(n, 0u);
   IntervalSet so, si;
   uint32_t cur = 0;
   bool staged = false, after_prev = false;
-  const bool check_live = opt_.mode == GPUOS_MODE_PERSISTENT && done_wm_ < next_seq_;
-  for (uint32_t r = 0; r < n; ++r) {
+  bool check_live = opt_.mode == GPUOS_MODE_PERSISTENT && done_wm_ < next_seq_;
+  // Fast path, one pass: outputs that follow one another in address order
+  // without overlap, and inputs whose hull no output touches, have no hazard
+  // (the usual shape of a stream of requests on slab-allocated tensors).
+  bool fast = true;
+  Extent oh{UINT64_MAX, 0}, ih{UINT64_MAX, 0};
+  uint64_t prev_hi = 0;
+  for (uint32_t r = 0; r < n && fast; ++r) {
     const Pending& p = reqs[i + r];
-    bool hz = so.overlaps(p.out_ext) || si.overlaps(p.out_ext);
-    for (int k = 0; k < p.nin && !hz; ++k) hz = so.overlaps(p.in_ext[k]);
-    if (hz) {
-      so.clear();
-      si.clear();
-      cur = r;
-      staged = true;
+    if (!p.out_ext.empty()) {
+      if (p.out_ext.lo < prev_hi) fast = false;
+      prev_hi = p.out_ext.hi;
+      oh.lo = std::min(oh.lo, p.out_ext.lo);
+      oh.hi = std::max(oh.hi, p.out_ext.hi);
     }
-    stage_first[r] = cur;
-    so.add(p.out_ext);
-    for (int k = 0; k < p.nin; ++k) si.add(p.in_ext[k]);
+    for (int k = 0; k < p.nin; ++k) {
+      if (p.in_ext[k].empty()) continue;
+      ih.lo = std::min(ih.lo, p.in_ext[k].lo);
+      ih.hi = std::max(ih.hi, p.in_ext[k].hi);
+    }
+  }
+  auto meets = [](const Extent& a, const Extent& b) {
+    return !a.empty() && !b.empty() && a.lo < b.hi && b.lo < a.hi;
+  };
+  if (fast && meets(oh, ih)) fast = false;
+  if (fast && check_live) {
+    // and none of the batches in flight writes what this one touches, or
+    // reads what it writes
+    const Extent lo_h = live_out_.hull(), li_h = live_in_.hull();
+    if (!meets(oh, lo_h) && !meets(ih, lo_h) && !meets(oh, li_h)) check_live = false;
+  }
+  for (uint32_t r = 0; r < n && (!fast || check_live); ++r) {
+    const Pending& p = reqs[i + r];
+    if (!fast) {
+      bool hz = so.overlaps(p.out_ext) || si.overlaps(p.out_ext);
+      for (int k = 0; k < p.nin && !hz; ++k) hz = so.overlaps(p.in_ext[k]);
+      if (hz) {
+        so.clear();
+        si.clear();
+        cur = r;
+        staged = true;
+      }
+      stage_first[r] = cur;
+      so.add(p.out_ext);
+      for (int k = 0; k < p.nin; ++k) si.add(p.in_ext[k]);
+    }
     if (check_live && !after_prev) {
       bool lz = live_out_.overlaps(p.out_ext) || live_in_.overlaps(p.out_ext);
       for (int k = 0; k < p.nin && !lz; ++k) lz = live_out_.overlaps(p.in_ext[k]);
@@ -893,16 +925,22 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   }
   // Within each stage the order of requests is free: group them by operator
   // so that the warps of an SM run few operator bodies at a time.
+  // (a stable counting sort on a 256-entry key: kind and variant)
   std::vector<uint32_t> order(n);
-  for (uint32_t r = 0; r < n; ++r) order[r] = r;
-  for (uint32_t s0 = 0; s0 < n;) {
-    uint32_t s1 = s0 + 1;
-    while (s1 < n && stage_first[s1] == stage_first[s0]) ++s1;
-    std::stable_sort(order.begin() + s0, order.begin() + s1, [&](uint32_t x, uint32_t y) {
-      const int kx = reqs[i + x].r.kind * 1024 + var[x], ky = reqs[i + y].r.kind * 1024 + var[y];
-      return kx < ky;
-    });
-    s0 = s1;
+  {
+    auto key = [&](uint32_t r) -> uint32_t {
+      return ((uint32_t)reqs[i + r].r.kind << 7) | ((uint32_t)var[r] & 127u);
+    };
+    uint32_t counts[257];
+    for (uint32_t s0 = 0; s0 < n;) {
+      uint32_t s1 = s0 + 1;
+      while (s1 < n && stage_first[s1] == stage_first[s0]) ++s1;
+      std::memset(counts, 0, sizeof(counts));
+      for (uint32_t r = s0; r < s1; ++r) ++counts[key(r) + 1];
+      for (int b = 0; b < 256; ++b) counts[b + 1] += counts[b];
+      for (uint32_t r = s0; r < s1; ++r) order[s0 + counts[key(r)]++] = r;
+      s0 = s1;
+    }
   }
   // payload layout
   std::vector<uint32_t> cb(n + 1);

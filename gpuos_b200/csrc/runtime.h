@@ -53,6 +53,8 @@ class IntervalSet {
   void add(Extent e);
   void clear() { v_.clear(); }
   bool empty() const { return v_.empty(); }
+  // the smallest extent covering the set (empty when the set is)
+  Extent hull() const { return v_.empty() ? Extent{} : Extent{v_.front().lo, v_.back().hi}; }
   size_t size() const { return v_.size(); }
 
  private:
