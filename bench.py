@@ -490,19 +490,23 @@ def profile_case(dev="cuda:0"):
     """The small case the committed ncu captures use: two stream-mode launches
     of gpuos_batch_kernel (one executor, batches of up to 2048 requests):
     2048 fp32 adds of 8192 elements (201 MB), then the first 2048 requests of
-    the mixed 24-operator stream.  A few GB on the device at most."""
+    the mixed 24-operator stream.  A 256 MB write before each launch evicts
+    its inputs from L2.  A few GB on the device at most."""
     import gpuos_b200.cabi as C
     from gpuos_b200 import workloads as W
+    scrub = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 2 x L2: evicts the inputs
     with C.Executor(0, mode=C.MODE_STREAM, max_batch=2048) as e:
         A = torch.randn(2048, 8192, device=dev)
         B = torch.randn(2048, 8192, device=dev)
         O = torch.empty(2048, 8192, device=dev)
-        for i in range(2048):
-            e.builtin(C.OP_ADD, A[i], B[i], O[i])
-        e.flush(sync=True)
         st = W.mixed_24op(n_req=2048, seed=0)
         din, dout = st.device_buffers(dev)
         calls = W.Submitter(_CabiExt(e)).prepare(st, st.views(din, dout))
+        scrub.fill_(1)
+        for i in range(2048):
+            e.builtin(C.OP_ADD, A[i], B[i], O[i])
+        e.flush(sync=True)
+        scrub.fill_(2)
         for fn, a in calls:
             fn(*a)
         e.flush(sync=True)

@@ -644,3 +644,66 @@ def test_custom_expression_ordering_and_hot_swap(mode):
         e.binary(0, ga, gb, w)
         e.flush(sync=True)
         assert torch.equal(w.cpu(), a + b)
+
+
+# ---------------------------------------------------------------------------
+# The transformer-decode pointwise chain (bf16): residual add, RMSNorm as
+# x*x -> mean(-1) -> +eps -> pow(-0.5) -> * rstd[b,1] -> * w[4096], bias, and
+# a SiLU-style gate (sigmoid, mul) on [b, 11008]; several layers in ONE flush,
+# so every step depends on the one before.
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("mode", MODES, ids=MODE_IDS)
+def test_decode_chain_bf16(mode):
+    bf = torch.bfloat16
+    B, H, F, L = 8, 4096, 11008, 3
+    g = torch.Generator().manual_seed(91)
+
+    def normal(*shape):
+        return (torch.randn(*shape, generator=g) * 0.02).to(bf)
+
+    with C.Executor(0, mode=mode) as e:
+        s_sig = slot_of(e, "sigmoid")
+        s_pow = slot_of(e, "pow")
+        s_mean = e.register_reduce("t|mean", "mean")
+        eps = gpu(torch.tensor(1e-6, dtype=bf))
+        nhalf = gpu(torch.tensor(-0.5, dtype=bf))
+        x = gpu(normal(B, H))
+        steps = []
+        for _ in range(L):
+            res, w, bias = gpu(normal(B, H)), gpu(normal(H)), gpu(normal(H))
+            u, u2 = gpu(normal(B, F)), gpu(normal(B, F))
+            nan = lambda *s: torch.full(s, float("nan"), dtype=bf, device=DEV)  # noqa: E731
+            h, sq, hn, hw, xo = nan(B, H), nan(B, H), nan(B, H), nan(B, H), nan(B, H)
+            ms, mse, rstd = nan(B, 1), nan(B, 1), nan(B, 1)
+            gt, act = nan(B, F), nan(B, F)
+            e.builtin(C.OP_ADD, x, res, h)
+            e.builtin(C.OP_MUL, h, h, sq)
+            e.reduce(s_mean, sq, ms, [1], True)
+            e.builtin(C.OP_ADD, ms, eps, mse)
+            e.binary(s_pow, mse, nhalf, rstd)
+            e.builtin(C.OP_MUL, h, rstd, hn)         # [b,H] * [b,1]
+            e.builtin(C.OP_MUL, hn, w, hw)           # [b,H] * [H]
+            e.builtin(C.OP_ADD, hw, bias, xo)
+            e.unary(s_sig, u, gt)
+            e.builtin(C.OP_MUL, gt, u2, act)
+            steps.append(dict(x=x, res=res, w=w, bias=bias, u=u, u2=u2, h=h, sq=sq, ms=ms,
+                              mse=mse, rstd=rstd, hn=hn, hw=hw, xo=xo, gt=gt, act=act))
+            x = xo
+        e.flush(sync=True)
+        for st in steps:
+            c = {k: v.cpu() for k, v in st.items()}
+            # every request against the oracle, from the inputs the GPU gave it
+            compare("add", c["x"], c["res"], c["h"])
+            compare("mul", c["h"], c["h"], c["sq"])
+            ref = torch.empty(B, 1)
+            oracle.reduce("mean", c["sq"].float(), ref, [1], True)
+            tol = 1e-5 * c["sq"].float().abs().sum(1, keepdim=True) + ref.abs() * 2 ** -8
+            assert bool(((c["ms"].float() - ref).abs() <= tol).all())
+            compare("add", c["ms"], torch.tensor(1e-6, dtype=bf), c["mse"])
+            compare("pow", c["mse"], torch.tensor(-0.5, dtype=bf), c["rstd"])
+            compare("mul", c["h"], c["rstd"], c["hn"])
+            compare("mul", c["hn"], c["w"], c["hw"])
+            compare("add", c["hw"], c["bias"], c["xo"])
+            compare("sigmoid", c["u"], None, c["gt"])
+            compare("mul", c["gt"], c["u2"], c["act"])
+            assert not torch.isnan(c["xo"].float()).any()
