@@ -54,8 +54,43 @@ def peaks():
 
 
 # ---------------------------------------------------------------------------
+_NVML_POLL = r"""
+import os, select, sys, time
+import pynvml as N
+os.nice(10)
+N.nvmlInit()
+try:
+    h = N.nvmlDeviceGetHandleByUUID(sys.argv[1])
+except N.NVMLError:
+    h = N.nvmlDeviceGetHandleByIndex(int(sys.argv[2]))
+period = float(sys.argv[3])
+bits = [("hw_slowdown", N.nvmlClocksEventReasonHwSlowdown),
+        ("hw_thermal_slowdown", N.nvmlClocksEventReasonHwThermalSlowdown),
+        ("sw_thermal_slowdown", N.nvmlClocksEventReasonSwThermalSlowdown),
+        ("sw_power_cap", N.nvmlClocksEventReasonSwPowerCap)]
+print("ready", N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM), flush=True)
+sys.stdin.readline()  # "go": the timed region has begun
+out = []
+while True:
+    t = time.monotonic()
+    sm = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+    r = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+    out.append(f"{t:.6f} {sm} " + (",".join(n for n, b in bits if r & b) or "-"))
+    if select.select([sys.stdin], [], [], period)[0]:
+        break
+print("\n".join(out), flush=True)
+"""
+
+
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+    """SM clocks and throttle reasons sampled while the timed region runs.
+
+    A helper process (niced) polls NVML every 20 ms with CLOCK_MONOTONIC time
+    stamps, from the moment start() tells it to go until stop(); only the
+    samples between the two count.  Polling in another process keeps it off
+    this process's interpreter lock, which the host-side submission loop
+    holds.  nvidia-smi (100 ms period) is the fallback.
+    """
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -64,31 +99,80 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.smi = None
         self.lines = []
+        self.max_mhz = None
 
     def start(self):
+        uuid = ""
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.index).uuid)
+        except (AttributeError, RuntimeError):
+            pass
         try:
             self.proc = subprocess.Popen(
+                [sys.executable, "-c", _NVML_POLL, uuid, str(self.index), "0.02"],
+                stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+            ready = self.proc.stdout.readline().split()
+            if len(ready) == 2 and ready[0] == "ready":
+                self.max_mhz = float(ready[1])
+            else:
+                self.proc.wait(timeout=5)
+                self.proc = None
+        except (OSError, subprocess.TimeoutExpired):
+            self.proc = None
+        self.t0 = time.monotonic()
+        if self.proc is not None:
+            try:
+                self.proc.stdin.write("go\n")
+                self.proc.stdin.flush()
+            except OSError:
+                self.proc = None
+        if self.proc is None:
+            self._start_smi()
+
+    def _start_smi(self):
+        try:
+            self.smi = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except OSError:
-            self.proc = None
+            self.smi = None
 
     def _read(self):
-        for line in self.proc.stdout:
+        for line in self.smi.stdout:
             self.lines.append(line.strip())
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
+        t1 = time.monotonic()
+        if self.proc is not None:
+            try:
+                out, _ = self.proc.communicate(input="stop\n", timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out = ""
+            sm, reasons = [], set()
+            for ln in out.splitlines():
+                f = ln.split()
+                if len(f) != 3 or not (self.t0 <= float(f[0]) <= t1):
+                    continue
+                sm.append(float(f[1]))
+                if f[2] != "-":
+                    reasons.update(f[2].split(","))
+            return {"sm_mhz": statistics.median(sm) if sm else None,
+                    "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                    "samples": len(sm), "source": "nvml, 20 ms"}
+        if not self.smi:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        self.smi.terminate()
         try:
-            self.proc.wait(timeout=5)
+            self.smi.wait(timeout=5)
         except subprocess.TimeoutExpired:
-            self.proc.kill()
+            self.smi.kill()
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
@@ -105,7 +189,7 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 100 ms"}
 
 
 # ---------------------------------------------------------------------------

@@ -290,150 +290,148 @@ __device__ __forceinline__ float vec_opnd1(int mode, uint64_t p, int dt, float s
   return sc;
 }
 
-// elements [e0, e0 + n) of a request whose operands are all linear or scalar
+// elements [e0, e0 + n) of a request whose operands are all linear or scalar.
+// The chunk is walked in whole groups of 4 elements, group q on lane q % 32:
+// each round loads up to kG groups per lane, each under its own bound, before
+// any is computed, so a chunk of any length costs one memory round trip per
+// kG x 128 elements; the last n % 4 elements (the ragged end of a request) go
+// one per lane.  Every group's registers are defined on every path (a load
+// under a predicate alone would keep them live across the loop's back edge).
 template <int V>
 __device__ __forceinline__ void ew_vec_flat(const VecView& u, float p0, float p1, int64_t e0,
                                             int64_t n, int lane) {
-  constexpr int64_t kStep = 4 * 32;
   constexpr int kG = vec_groups<V>();
   const bool as = u.ma == OM_SCALAR, bs = u.mb == OM_SCALAR;
-  int64_t i = 4 * (int64_t)lane;
+  const int64_t nq = n >> 2;
 #pragma unroll 1
-  for (; i + kStep * (kG - 1) + 4 <= n; i += kStep * kG) {
+  for (int64_t q0 = lane; q0 < nq; q0 += 32 * kG) {
+    const int64_t eb = e0 + 4 * q0;   // this lane's first element of the round
+    const int left = (int)(nq - q0);  // groups from there to the chunk's end
     float A[kG][4], B[kG][4];
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
-      const int64_t e = e0 + i + kStep * g;
-      if (as) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) A[g][k] = u.As;
-      } else {
-        ld4(u.a, u.dta, e, A[g]);
+      for (int k = 0; k < 4; ++k) {
+        A[g][k] = u.As;
+        B[g][k] = u.Bs;
       }
-      if (bs) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) B[g][k] = u.Bs;
-      } else {
-        ld4(u.b, u.dtb, e, B[g]);
+      if (32 * g < left) {
+        if (!as) ld4(u.a, u.dta, eb + 128 * g, A[g]);
+        if (!bs) ld4(u.b, u.dtb, eb + 128 * g, B[g]);
       }
     }
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
-      float R[4];
-      op4<V>(A[g], B[g], R, p0, p1);
-      st4(u.o, u.dto, e0 + i + kStep * g, R);
-    }
-  }
-#pragma unroll 1
-  for (; i < n; i += kStep) {
-    const int64_t e = e0 + i;
-    if (i + 4 <= n) {
-      float A[4], B[4], R[4];
-      vec_opnd4(u.ma, u.a, u.dta, u.As, e, 0, 0, A);
-      vec_opnd4(u.mb, u.b, u.dtb, u.Bs, e, 0, 0, B);
-      op4<V>(A, B, R, p0, p1);
-      st4(u.o, u.dto, e, R);
-    } else {
-      for (int64_t k = 0; k < n - i; ++k) {
-        const float A = vec_opnd1(u.ma, u.a, u.dta, u.As, e + k, 0, 0);
-        const float B = vec_opnd1(u.mb, u.b, u.dtb, u.Bs, e + k, 0, 0);
-        st1(u.o, u.dto, e + k, op1<V>(A, B, p0, p1));
+      if (32 * g < left) {
+        float R[4];
+        op4<V>(A[g], B[g], R, p0, p1);
+        st4(u.o, u.dto, eb + 128 * g, R);
       }
     }
+  }
+  if (lane < (int)(n & 3)) {
+    const int64_t e = e0 + 4 * nq + lane;
+    const float A = vec_opnd1(u.ma, u.a, u.dta, u.As, e, 0, 0);
+    const float B = vec_opnd1(u.mb, u.b, u.dtb, u.Bs, e, 0, 0);
+    st1(u.o, u.dto, e, op1<V>(A, B, p0, p1));
   }
 }
 
 // elements [e0, e0 + n) of a request with a per-row operand or output
-// (rows of u.inner elements, a multiple of 4)
+// (rows of u.inner elements, a multiple of 4, so a group of 4 never straddles
+// two rows); walked in predicated groups as ew_vec_flat.
 template <int V>
 __device__ __forceinline__ void ew_vec_rows(const VecView& u, float p0, float p1, int64_t e0,
                                             int64_t n, int lane) {
-  constexpr int64_t kStep = 4 * 32;
   constexpr int kG = op_unroll<V>() == 2 ? 4 : 2;
-  int64_t i = 4 * (int64_t)lane;
+  const int64_t nq = n >> 2;
 #pragma unroll 1
-  for (; i + kStep * (kG - 1) + 4 <= n; i += kStep * kG) {
+  for (int64_t q0 = lane; q0 < nq; q0 += 32 * kG) {
+    const int64_t eb = e0 + 4 * q0;
+    const int left = (int)(nq - q0);
     float A[kG][4], B[kG][4];
     int64_t oo[kG];
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
-      const int64_t e = e0 + i + kStep * g;
+      const int64_t e = eb + 128 * g;
       const int64_t r = vec_row(u, e), c = e - r * u.inner;
-      vec_opnd4(u.ma, u.a, u.dta, u.As, e, r * u.sa_row, c, A[g]);
-      vec_opnd4(u.mb, u.b, u.dtb, u.Bs, e, r * u.sb_row, c, B[g]);
       oo[g] = u.mo ? r * u.so_row + c : e;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        A[g][k] = u.As;
+        B[g][k] = u.Bs;
+      }
+      if (32 * g < left) {
+        vec_opnd4(u.ma, u.a, u.dta, u.As, e, r * u.sa_row, c, A[g]);
+        vec_opnd4(u.mb, u.b, u.dtb, u.Bs, e, r * u.sb_row, c, B[g]);
+      }
     }
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
-      float R[4];
-      op4<V>(A[g], B[g], R, p0, p1);
-      st4(u.o, u.dto, oo[g], R);
-    }
-  }
-#pragma unroll 1
-  for (; i < n; i += kStep) {
-    const int64_t e = e0 + i;
-    if (i + 4 <= n) {
-      const int64_t r = vec_row(u, e), c = e - r * u.inner;
-      float A[4], B[4], R[4];
-      vec_opnd4(u.ma, u.a, u.dta, u.As, e, r * u.sa_row, c, A);
-      vec_opnd4(u.mb, u.b, u.dtb, u.Bs, e, r * u.sb_row, c, B);
-      op4<V>(A, B, R, p0, p1);
-      st4(u.o, u.dto, u.mo ? r * u.so_row + c : e, R);
-    } else {
-      // ragged end of a request: fewer than 4 elements
-      for (int64_t k = 0; k < n - i; ++k) {
-        const int64_t ek = e + k;
-        const int64_t r = vec_row(u, ek), c = ek - r * u.inner;
-        const float A = vec_opnd1(u.ma, u.a, u.dta, u.As, ek, r * u.sa_row, c);
-        const float B = vec_opnd1(u.mb, u.b, u.dtb, u.Bs, ek, r * u.sb_row, c);
-        st1(u.o, u.dto, u.mo ? r * u.so_row + c : ek, op1<V>(A, B, p0, p1));
+      if (32 * g < left) {
+        float R[4];
+        op4<V>(A[g], B[g], R, p0, p1);
+        st4(u.o, u.dto, oo[g], R);
       }
     }
+  }
+  if (lane < (int)(n & 3)) {
+    const int64_t ek = e0 + 4 * nq + lane;
+    const int64_t r = vec_row(u, ek), c = ek - r * u.inner;
+    const float A = vec_opnd1(u.ma, u.a, u.dta, u.As, ek, r * u.sa_row, c);
+    const float B = vec_opnd1(u.mb, u.b, u.dtb, u.Bs, ek, r * u.sb_row, c);
+    st1(u.o, u.dto, u.mo ? r * u.so_row + c : ek, op1<V>(A, B, p0, p1));
   }
 }
 
 // All-fp32 flat requests (the common case) run a body with no dtype
 // branches: its code is a fraction of the general one's, which keeps the
-// instruction cache warm when a batch mixes operators.
+// instruction cache warm when a batch mixes operators.  Same walk in
+// predicated groups as ew_vec_flat.
 template <int V>
 __device__ __forceinline__ void ew_vec_f32(const VecView& u, float p0, float p1, int64_t e0,
                                            int64_t n, int lane) {
-  constexpr int64_t kStep = 4 * 32;
   constexpr int kG = vec_groups<V>();
-  const float* A = reinterpret_cast<const float*>(u.a);
-  const float* B = reinterpret_cast<const float*>(u.b);
-  float* O = reinterpret_cast<float*>(u.o);
   const bool as = u.ma == OM_SCALAR, bs = u.mb == OM_SCALAR;
-  int64_t i = 4 * (int64_t)lane;
+  const int64_t nq = n >> 2;
 #pragma unroll 1
-  for (; i + kStep * (kG - 1) + 4 <= n; i += kStep * kG) {
+  for (int64_t q0 = lane; q0 < nq; q0 += 32 * kG) {
+    const int64_t eb = e0 + 4 * q0;
+    const int left = (int)(nq - q0);
+    const float4* A = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(u.a) + eb);
+    const float4* B = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(u.b) + eb);
+    float4* O = reinterpret_cast<float4*>(reinterpret_cast<float*>(u.o) + eb);
+    // every group is defined on every path (a load under a predicate alone
+    // would keep the registers live across the loop's back edge)
     float4 a[kG], b[kG];
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
-      const int64_t e = e0 + i + kStep * g;
-      a[g] = as ? make_float4(u.As, u.As, u.As, u.As) : *reinterpret_cast<const float4*>(A + e);
-      b[g] = bs ? make_float4(u.Bs, u.Bs, u.Bs, u.Bs) : *reinterpret_cast<const float4*>(B + e);
+      a[g] = make_float4(u.As, u.As, u.As, u.As);
+      b[g] = make_float4(u.Bs, u.Bs, u.Bs, u.Bs);
+      if (32 * g < left) {
+        if (!as) a[g] = A[32 * g];
+        if (!bs) b[g] = B[32 * g];
+      }
     }
 #pragma unroll
     for (int g = 0; g < kG; ++g) {
-      float4 r;
-      r.x = op1<V>(a[g].x, b[g].x, p0, p1);
-      r.y = op1<V>(a[g].y, b[g].y, p0, p1);
-      r.z = op1<V>(a[g].z, b[g].z, p0, p1);
-      r.w = op1<V>(a[g].w, b[g].w, p0, p1);
-      *reinterpret_cast<float4*>(O + e0 + i + kStep * g) = r;
+      if (32 * g < left) {
+        float4 r;
+        r.x = op1<V>(a[g].x, b[g].x, p0, p1);
+        r.y = op1<V>(a[g].y, b[g].y, p0, p1);
+        r.z = op1<V>(a[g].z, b[g].z, p0, p1);
+        r.w = op1<V>(a[g].w, b[g].w, p0, p1);
+        O[32 * g] = r;
+      }
     }
   }
-#pragma unroll 1
-  for (; i < n; i += kStep) {
-    const int64_t e = e0 + i;
-    const int64_t m = n - i < 4 ? n - i : 4;
-    for (int64_t k = 0; k < m; ++k) {
-      const float x = as ? u.As : A[e + k];
-      const float y = bs ? u.Bs : (u.mb == OM_LINEAR ? B[e + k] : 0.f);
-      O[e + k] = op1<V>(x, y, p0, p1);
-    }
+  if (lane < (int)(n & 3)) {
+    const int64_t e = e0 + 4 * nq + lane;
+    const float* A = reinterpret_cast<const float*>(u.a);
+    const float* B = reinterpret_cast<const float*>(u.b);
+    const float x = as ? u.As : A[e];
+    const float y = bs ? u.Bs : (u.mb == OM_LINEAR ? B[e] : 0.f);
+    reinterpret_cast<float*>(u.o)[e] = op1<V>(x, y, p0, p1);
   }
 }
 

@@ -251,6 +251,63 @@ def test_dtype_casts_bit_exact(op, dts):
                                ref.view(torch.int16 if do != torch.float32 else torch.int32)), (op, dts)
 
 
+@pytest.mark.parametrize("dts", [("f32", "f32", "f32"), ("f16", "f32", "f32"),
+                                 ("bf16", "bf16", "bf16")])
+def test_vector_rounds_end_inside_the_request(dts):
+    """The vector bodies walk a chunk in rounds of up to 8 (light) or 2
+    (heavy) groups of 4 elements per lane, each group under its own bound:
+    lengths just around the round and chunk boundaries, in one flush of small
+    requests (512-element chunks) and one with multi-million-element requests
+    (8192-element chunks), flat, with a scalar operand and with a per-row
+    operand.  Every result is checked against the oracle and the 64 elements
+    after each output must keep their sentinel."""
+    D = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+    da, db, do = (D[x] for x in dts)
+    g = torch.Generator().manual_seed(17)
+    flushes = [
+        [3, 4, 5, 124, 127, 128, 131, 1020, 1023, 1024, 1028, 4100, 8190, 8196, 40004, 70001],
+        [6_000_003, 1_000_001, 77],
+    ]
+    with C.Executor(0, mode=C.MODE_STREAM) as e:
+        s_exp = slot_of(e, "exp")
+        for sizes in flushes:
+            cases = []
+
+            def out(n):
+                buf = torch.full((n + 64,), 1234.5, dtype=do, device=DEV)
+                return buf, buf[:n]
+
+            for n in sizes:
+                a = torch.randn(n, generator=g).to(da)
+                b = torch.randn(n, generator=g).to(db)
+                ga, gb = gpu(a), gpu(b)
+                buf, go = out(n)
+                e.builtin(C.OP_ADD, ga, gb, go)
+                cases.append(("add", a, b, buf, n, ga, gb))
+                buf, go = out(n)
+                e.unary(s_exp, ga, go)
+                cases.append(("exp", a, None, buf, n, ga, None))
+                sc = torch.tensor(0.75, dtype=db)
+                gsc = gpu(sc)
+                buf, go = out(n)
+                e.builtin(C.OP_MUL, ga, gsc, go)
+                cases.append(("mul", a, sc, buf, n, ga, gsc))
+            for R, N in ((1, 4), (3, 132), (37, 1028), (5, 8196)):
+                a = torch.randn(R, N, generator=g).to(da)
+                b = torch.randn(N, generator=g).to(db)
+                ga, gb = gpu(a), gpu(b)
+                buf = torch.full((R * N + 64,), 1234.5, dtype=do, device=DEV)
+                e.builtin(C.OP_SUB, ga, gb, buf[:R * N].view(R, N))
+                cases.append(("sub", a, b, buf, R * N, ga, gb))
+            e.flush(sync=True)
+            sentinel = torch.full((64,), 1234.5, dtype=do)
+            for op, a, b, buf, n, _, _ in cases:
+                got = buf.cpu()
+                where = f" n={n} {dts}"
+                assert torch.equal(_bits(got[n:]), _bits(sentinel)), f"{op}{where}: wrote past the end"
+                compare(op, a, b, got[:n].view(a.shape), where=where)
+
+
 # --------------------------------------------------------------------------
 # broadcast, views, strided layouts
 # --------------------------------------------------------------------------
