@@ -10,10 +10,12 @@
 //  * Aligned elementwise chunks run the vector body (ew_vec: 128-bit loads,
 //    up to 8 groups of 4 elements per lane in flight); strided views and
 //    reductions run the general warp bodies of executor.cuh.
-//  * Completion: each warp fences its stores, the CTA adds its chunk count to
-//    the batch's done counter once, and the CTA that completes the batch posts
-//    the completion word.  The last CTA to leave the batch marks its payload
-//    reusable (retired).
+//  * Completion: in the persistent worker each warp fences its stores, the
+//    CTA adds its chunk count to the batch's done counter once, and the CTA
+//    that completes the batch posts the completion word; the last CTA to leave
+//    the batch marks its payload reusable (retired).  A stream-mode launch of a
+//    batch without stage barriers has no such protocol: the event recorded
+//    after it completes the batch, and a warp that meets an error posts it.
 //  * A batch with stage barriers (a request that depends on an earlier one)
 //    hands granules out in order with an atomic instead, counts chunks one by
 //    one, and a chunk of a later stage waits (bounded) until every chunk of

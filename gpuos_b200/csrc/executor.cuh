@@ -166,8 +166,18 @@ struct Exec {
   int lane;
 };
 
+// A stream-mode batch without stage barriers has no end-of-batch protocol
+// (the event recorded after its launch completes it), so an error is posted
+// to the host at once: the completion word with the bits this warp knows; the
+// host reads the batch's full error bits from `st` after the kernel.
+__device__ __forceinline__ bool posts_own_errors(const Exec& ex) {
+  return !ex.done_dev && !(ex.flags & BF_STAGED);
+}
+
 __device__ __forceinline__ void set_err(const Exec& ex, uint32_t bits) {
   atomicOr(&ex.st->err, bits);
+  if (posts_own_errors(ex))
+    ex.done_ring[ex.seq % kDoneRing] = (ex.seq + 1) | ((uint64_t)(bits & 0xffu) << 48);
 }
 
 // ---------------------------------------------------------------------------

@@ -174,11 +174,12 @@ JitKernel jit_link(const std::vector<char>& ops_cubin) {
     cu_check(linkComplete(ls, &out, &outsz), "cuLinkComplete");
     CUmodule mod = nullptr;
     cu_check(moduleLoad(&mod, out), "cuModuleLoadData");
+    k.module = mod;
     CUfunction fn = nullptr;
     cu_check(getFunction(&fn, mod, "gpuos_jit_batch_kernel"), "cuModuleGetFunction");
-    k.module = mod;
     k.function = fn;
   } catch (...) {
+    if (k.module) driver_fn<CUresult (*)(CUmodule)>("cuModuleUnload")(static_cast<CUmodule>(k.module));
     linkDestroy(ls);
     throw;
   }

@@ -30,6 +30,9 @@ gpuos_batch_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
   const int warp = threadIdx.x >> 5;
   const uint32_t count = warp_batch(ex, blockIdx.x * kWarpsPerCta + warp,
                                     gridDim.x * kWarpsPerCta, &ext[warp]);
+  // without stage barriers nothing waits on the batch's counters: the kernel's
+  // completion completes the batch, and its warps leave as soon as they are done
+  if (posts_own_errors(ex)) return;
   cta_leave_batch(ex, &cta_chunks, count, gridDim.x, nullptr);
 }
 

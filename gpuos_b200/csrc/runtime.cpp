@@ -765,6 +765,7 @@ void Executor::reclaim() {
       } else {
         const uint64_t w = done_ring_[done_wm_ % kDoneRing];
         e = (w & kDoneMask) == done_wm_ + 1 ? (uint32_t)((w >> 48) & 0xffu) : 0u;
+        if (e) e |= take_batch_err(done_wm_);
       }
       if (e) {
         ++errors_;
@@ -797,6 +798,23 @@ void Executor::reclaim() {
     live_out_.clear();
     live_in_.clear();
   }
+}
+
+// A stream-mode batch that posted an error word itself (no end-of-batch
+// protocol ran): its complete error bits are in its device counters; read
+// them and clear the slot for its next use.  Only runs for failed batches.
+uint32_t Executor::take_batch_err(uint64_t seq) {
+  DeviceGuard g(device_);
+  BatchState st;
+  std::memset(&st, 0, sizeof(st));
+  BatchState* d = states_ + seq % kDoneRing;
+  if (cudaMemcpyAsync(&st, d, sizeof(st), cudaMemcpyDeviceToHost, s_ctrl_) != cudaSuccess ||
+      cudaMemsetAsync(d, 0, sizeof(st), s_ctrl_) != cudaSuccess ||
+      cudaStreamSynchronize(s_ctrl_) != cudaSuccess) {
+    if (cuda_err_.empty()) cuda_err_ = "reading a failed batch's error bits";
+    return ERR_CUDA;
+  }
+  return st.err;
 }
 
 bool Executor::wait_for_room_locked(std::unique_lock<std::mutex>& lk, uint64_t bytes,

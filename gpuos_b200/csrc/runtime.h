@@ -136,6 +136,7 @@ class Executor {
  private:
   void publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& reqs, size_t i, size_t j,
                cudaStream_t stream);
+  uint32_t take_batch_err(uint64_t seq);
   void reclaim();
   void ensure_worker_locked();
   void launch_worker_locked(uint64_t start);

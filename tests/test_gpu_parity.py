@@ -542,6 +542,13 @@ def test_unregistered_slot_reports_error(ex):
     ex.builtin(C.OP_ADD, x, x, y)           # the executor stays usable
     ex.flush(sync=True)
     assert torch.equal(y, x + x)
+    # the failed batch's counter slot comes round again (1024 slots) clean
+    z = torch.empty_like(x)
+    for i in range(1030):
+        ex.builtin(C.OP_MUL if i % 2 else C.OP_ADD, x, x, z)
+        ex.flush(sync=False)
+    ex.flush(sync=True)
+    assert torch.equal(z, x * x)  # the last one (i = 1029) multiplies
 
 
 def test_bad_requests_rejected_on_host(ex):
