@@ -367,12 +367,17 @@ def flush_latency(ext, dev, reps=400):
 
 
 def roofline_leg(stream, dev, steps, peak_gbs, peak_kind):
-    """Per-launch CUDA-event timing of the batch kernel (stream mode).
+    """Launch duration of the batch kernel (stream mode) and its roofline.
 
     Each step's requests are queued first; the stream is then held by a short
     spin kernel while one flush publishes the step's batches (512 requests
-    each, as in the main run), so that the launches run back to back and each
-    event pair around a launch times the kernel, not the host's launch latency.
+    each, as in the main run), so that the launches run back to back.  One
+    event pair brackets each step's launches (recorded after the spin): the
+    average launch duration is that region's time over the launches in it,
+    gaps between launches included.  A second pass brackets every launch with
+    its own event pair (`per_launch_event_us`); on this GPU an event pair
+    around a single launch costs several microseconds by itself (about 6 us
+    around an empty kernel), so that figure is an upper bound.
     """
     import gpuos_b200.cabi as C
     from gpuos_b200 import workloads as W
@@ -387,28 +392,47 @@ def roofline_leg(stream, dev, steps, peak_gbs, peak_kind):
         batch_bytes = []
         for i in range(0, len(stream.requests), fe):
             batch_bytes.append(sum(r.algo_bytes for r in stream.requests[i:i + fe]))
-        cs = torch.cuda.current_stream().cuda_stream
+        per = len(batch_bytes)
+        cur = torch.cuda.current_stream()
+        cs = cur.cuda_stream
+        region_s, launches = 0.0, 0
+        for s in range(steps + 1):
+            for fn, a in calls:
+                fn(*a)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(8_000_000)  # a few ms: longer than publishing the step
+            e0.record(cur)
+            q0 = ex.stats()["published"]
+            ex.flush(sync=False, stream=cs)
+            e1.record(cur)
+            n = ex.stats()["published"] - q0
+            ex.flush(sync=True, stream=cs)
+            assert n == per, (n, per)
+            if s >= 1:
+                region_s += e0.elapsed_time(e1) / 1e3
+                launches += n
+        # second pass: an event pair around every launch
         ex.set_timing(True)
         for s in range(steps + 1):
             if s == 1:
                 ex.take_timings()
             for fn, a in calls:
                 fn(*a)
-            torch.cuda._sleep(8_000_000)  # a few ms: longer than publishing the step
+            torch.cuda._sleep(8_000_000)
             ex.flush(sync=False, stream=cs)
             ex.flush(sync=True, stream=cs)
         ms = ex.take_timings()
-        per = len(batch_bytes)
         assert len(ms) == steps * per, (len(ms), steps, per)
         tot_bytes = sum(batch_bytes) * steps
-        tot_s = sum(ms) / 1e3
-        achieved = tot_bytes / tot_s / 1e9
+        achieved = tot_bytes / region_s / 1e9
         return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs,
                 "unit": "GB/s", "frac": round(achieved / peak_gbs, 4), "peak_kind": peak_kind,
                 "kernel": "gpuos_batch_kernel",
-                "avg_launch_us": round(sum(ms) / len(ms) * 1e3, 2),
+                "avg_launch_us": round(region_s / launches * 1e6, 2),
+                "per_launch_event_us": round(sum(ms) / len(ms) * 1e3, 2),
                 "bytes_per_launch": int(sum(batch_bytes) / per),
-                "launches": len(ms), "traffic": None}
+                "launches": launches, "traffic": None}
     finally:
         ex.close()
 

@@ -357,6 +357,7 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   GCU(cudaStreamCreateWithFlags(&s_worker_, cudaStreamNonBlocking));
   GCU(cudaStreamCreateWithFlags(&s_ctrl_, cudaStreamNonBlocking));
   GCU(cudaStreamCreateWithFlags(&s_own_, cudaStreamNonBlocking));
+  GCU(cudaStreamCreateWithFlags(&s_copy_, cudaStreamNonBlocking));
   GCU(cudaEventCreateWithFlags(&last_event_, cudaEventDisableTiming));
 
   // staging arena (pinned, mapped) and its device mirror
@@ -1089,7 +1090,22 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       GCU(cudaEventRecord(last_event_, last_stream_));
       GCU(cudaStreamWaitEvent(stream, last_event_, 0));
     }
-    GCU(cudaMemcpyAsync(ring_ + aoff, arena_ + aoff, bytes, cudaMemcpyHostToDevice, stream));
+    // The payload is copied on the executor's copy stream, which the launch
+    // waits on: the copy runs while the caller's stream is still busy with
+    // earlier work, instead of in front of this kernel.  (Its ring space was
+    // freed only after the kernel that used it before had completed.)  A
+    // stream being captured into a graph copies in line.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    GCU(cudaStreamIsCapturing(stream, &cap));
+    if (cap == cudaStreamCaptureStatusNone) {
+      cudaEvent_t& ce = copy_ev_[seq % kDoneRing];
+      if (!ce) GCU(cudaEventCreateWithFlags(&ce, cudaEventDisableTiming));
+      GCU(cudaMemcpyAsync(ring_ + aoff, arena_ + aoff, bytes, cudaMemcpyHostToDevice, s_copy_));
+      GCU(cudaEventRecord(ce, s_copy_));
+      GCU(cudaStreamWaitEvent(stream, ce, 0));
+    } else {
+      GCU(cudaMemcpyAsync(ring_ + aoff, arena_ + aoff, bytes, cudaMemcpyHostToDevice, stream));
+    }
     const uint64_t wpc = (uint64_t)block_ / 32;
     int grid = (int)std::min<uint64_t>((uint64_t)sm_count_ * batch_bps_, (ngran + wpc - 1) / wpc);
     grid = std::max(grid, 1);
@@ -1507,6 +1523,7 @@ void Executor::shutdown() {
   }
   cudaStreamSynchronize(s_own_);
   cudaStreamSynchronize(s_ctrl_);
+  if (s_copy_) cudaStreamSynchronize(s_copy_);
   if (states_) cudaFree(states_);
   for (JitKernel& k : jit_kernels_) jit_unload(k);
   jit_kernels_.clear();
@@ -1517,6 +1534,8 @@ void Executor::shutdown() {
   if (ring_) cudaFree(ring_);
   if (dctrl_) cudaFree(dctrl_);
   for (cudaEvent_t& e : done_ev_)
+    if (e) cudaEventDestroy(e);
+  for (cudaEvent_t& e : copy_ev_)
     if (e) cudaEventDestroy(e);
   if (partials_) cudaFree(partials_);
   if (counters_) cudaFree(counters_);
@@ -1533,6 +1552,8 @@ void Executor::shutdown() {
   if (s_worker_) cudaStreamDestroy(s_worker_);
   if (s_ctrl_) cudaStreamDestroy(s_ctrl_);
   if (s_own_) cudaStreamDestroy(s_own_);
+  if (s_copy_) cudaStreamDestroy(s_copy_);
+  s_copy_ = nullptr;
   states_ = nullptr; ring_ = nullptr; dctrl_ = nullptr; partials_ = nullptr; counters_ = nullptr;
   arena_ = nullptr; hostblk_ = nullptr; last_event_ = nullptr;
   s_worker_ = s_ctrl_ = s_own_ = nullptr;

@@ -156,6 +156,8 @@ class Executor {
   double sync_timeout_s_ = 60.0;
 
   cudaStream_t s_worker_ = nullptr, s_ctrl_ = nullptr, s_own_ = nullptr;
+  // stream mode: payload copies run here, ahead of the launch stream
+  cudaStream_t s_copy_ = nullptr;
 
   // mapped pinned host memory
   uint8_t* arena_ = nullptr;
@@ -194,6 +196,7 @@ class Executor {
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> timed_;
   std::vector<cudaEvent_t> ev_pool_;
   std::vector<cudaEvent_t> done_ev_ = std::vector<cudaEvent_t>(kDoneRing, nullptr);  // stream mode
+  std::vector<cudaEvent_t> copy_ev_ = std::vector<cudaEvent_t>(kDoneRing, nullptr);  // stream mode
   std::string cuda_err_;        // first CUDA error a completion query reported
 
   Tables tab_;
