@@ -111,14 +111,25 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
   uint2 g = make_uint2(0u, 0u);
   uint4 gw_rec = make_uint4(0u, 0u, 0u, 0u);
   uint32_t g_end = 0;
+  // static order: the entry of the granule after the next one is loaded an
+  // iteration ahead, so that the next granule's record load never waits on it
+  uint2 gq = make_uint2(0u, 0u);
   if (j < ngran) {
     g = __ldcg(ex.gtab + j);
+    if (!staged && j + W < ngran) gq = __ldcg(ex.gtab + j + W);
     gw_rec = load_req_words(ex.recs + g.x, lane);
     g_end = __ldcg(ex.gcb + g.x + 1);
   }
   while (j < ngran) {
     const uint32_t jn = staged ? claim() : j + W;  // the next granule, known ahead
-    const uint2 gn = jn < ngran ? __ldcg(ex.gtab + jn) : make_uint2(0u, 0u);
+    uint2 gn;
+    if (staged) {
+      gn = jn < ngran ? __ldcg(ex.gtab + jn) : make_uint2(0u, 0u);
+    } else {
+      gn = gq;
+      const uint32_t jq = jn + W;
+      gq = jq < ngran ? __ldcg(ex.gtab + jq) : make_uint2(0u, 0u);
+    }
     uint32_t c = j * G;
     const uint32_t cend = min(c + G, nchunk);
     if ((int)g.x != r) {

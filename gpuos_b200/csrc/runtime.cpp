@@ -184,10 +184,24 @@ void RingAlloc::free_before(uint64_t upto) {
   while (!live_.empty() && live_.front().tag < upto) live_.pop_front();
 }
 
-// Transcendental operators: compute-heavy chunks, sized smaller.
-bool is_heavy(int v) {
-  return v == V_POW || v == V_SIGMOID || v == V_TANH || v == V_EXP || v == V_LOG ||
-         v == V_GELU || v == V_SIN || v == V_COS || v == V_ELU || v == V_SOFTPLUS;
+// Relative time per element of an operator's vector body, from per-chunk
+// timings of a mixed batch on B200 (light operators 1): a chunk of operator v
+// gets 1/chunk_weight(v) of the light operators' elements, so that chunks of
+// every operator take about the same time and a batch's slowest warp is not
+// the one that drew two transcendental chunks.  The weight-2 operators also
+// run the 2-group vector body (op_unroll).
+int chunk_weight(int v) {
+  switch (v) {
+    case V_POW:
+      return 8;
+    case V_SIGMOID: case V_LOG: case V_SIN: case V_COS: case V_SOFTPLUS:
+      return 4;
+    case V_TANH: case V_EXP: case V_GELU: case V_ELU: case V_DIV: case V_DIV0: case V_SQRT:
+    case V_HARDSWISH:
+      return 2;
+    default:
+      return v >= V_JIT_BASE ? 4 : 1;
+  }
 }
 
 // Operator names accepted by gpuos_variant_by_name (and the Python layer).
@@ -913,16 +927,12 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       after_prev = lz;
     }
   }
-  // Elementwise chunk size for this batch: about two chunks per resident warp
-  // (multiple of 512 elements, 512..8192), half of that for the
-  // transcendental operators, whose chunks take longer.
-  uint64_t ew_elems = 0;
-  for (uint32_t r = 0; r < n; ++r)
-    if (reqs[i + r].r.kind == RK_EW) ew_elems += (uint64_t)reqs[i + r].r.numel;
-  const uint64_t warps = (uint64_t)std::max(1, total_warps_);
-  uint64_t ce = align_up(std::max<uint64_t>(1, ew_elems / (2 * warps)), 512);
-  ce = std::min<uint64_t>(std::max<uint64_t>(ce, 512), 8192);
+  // Elementwise chunk size for this batch: about two light-operator chunks'
+  // worth of work per resident warp (multiple of 512 elements, 512..8192),
+  // counting each element at its operator's chunk weight; an operator's
+  // chunks get 1/weight of that (at least 128 elements).
   std::vector<int> var(n);
+  uint64_t ew_work = 0;
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + r];
     int v = p.r.op;
@@ -932,8 +942,16 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       v = (phys >= 0 && phys < kMaxSlots) ? tab_.slot[phys].variant : V_NONE;
     }
     var[r] = v;
+    if (p.r.kind == RK_EW) ew_work += (uint64_t)p.r.numel * (uint64_t)chunk_weight(v);
+  }
+  const uint64_t warps = (uint64_t)std::max(1, total_warps_);
+  uint64_t ce = align_up(std::max<uint64_t>(1, ew_work / (2 * warps)), 512);
+  ce = std::min<uint64_t>(std::max<uint64_t>(ce, 512), 8192);
+  for (uint32_t r = 0; r < n; ++r) {
+    Pending& p = reqs[i + r];
+    const int v = var[r];
     if (p.r.kind != RK_EW) continue;
-    uint64_t c = is_heavy(v) ? std::max<uint64_t>(512, ce / 2) : ce;
+    uint64_t c = std::max<uint64_t>(128, ce / (uint64_t)chunk_weight(v));
     if (p.r.layout == EL_STRIDED) c = std::min<uint64_t>(c, 2048);
     // equal chunks (a multiple of 4 elements, as the vector path needs)
     const uint64_t numel = (uint64_t)p.r.numel;

@@ -229,7 +229,7 @@ void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
 
 // helpers shared with the tests of the host logic
 uint32_t fdiv_magic(uint32_t d, uint32_t* shift);
-bool is_heavy(int variant);
+int chunk_weight(int variant);
 int variant_by_name(const std::string& name);
 // Match an fp32 expression against the reference scheduler's expression
 // table; returns the variant (and parameters) or -1.
