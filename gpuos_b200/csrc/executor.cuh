@@ -182,41 +182,72 @@ __device__ __forceinline__ void set_err(const Exec& ex, uint32_t bits) {
 
 // ---------------------------------------------------------------------------
 // Elementwise generic path (one shared body): misaligned views, arbitrary
-// inner strides, and general strided requests of up to 8 dims.
+// inner strides, and general strided requests of up to 8 dims.  Each round a
+// lane computes the offsets of K elements (lane, lane + 32, ...) and issues
+// all their loads, raw, before converting or computing any, so that a chunk
+// costs one memory round trip per 32 K elements: one element at a time would
+// wait a full round trip each, since a store may alias the next load.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void ew_generic(const ReqView& q, const ExtRec* x, int v, float p0,
                                            float p1, int64_t e0, int64_t e1, int lane) {
+  constexpr int K = 4;
   const bool hasb = q.flags & RF_HAS_B;
   const int lay = q.layout;
   const int64_t N = q.inner;
-  for (int64_t e = e0 + lane; e < e1; e += 32) {
-    int64_t oa, ob, oo;
-    if (lay == EL_CONTIG) {
-      oa = (q.flags & RF_A_SCALAR) ? 0 : e;
-      ob = (q.flags & RF_B_SCALAR) ? 0 : e;
-      oo = e;
-    } else if (lay == EL_ROW2D) {
-      const int64_t r = row_of(q, e), c = e - r * N;
-      oa = r * q.sa_row + c * q.sa_in;
-      ob = r * q.sb_row + c * q.sb_in;
-      oo = r * q.so_row + c;
-    } else {
-      int64_t rem = e;
-      oa = ob = oo = 0;
-      for (int d = x->ndim - 1; d >= 0; --d) {
-        const int64_t sz = x->sizes[d];
-        const int64_t i = rem % sz;
-        rem /= sz;
-        oa += i * x->sa[d];
-        ob += i * x->sb[d];
-        oo += i * x->so[d];
+#pragma unroll 1
+  for (int64_t eb = e0 + lane; eb < e1; eb += 32 * K) {
+    // the offsets and raw bits of this lane's K elements of the round
+    uint32_t ra[K], rb[K];
+    int64_t oo[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t e = eb + 32 * k;
+      ra[k] = 0u;
+      rb[k] = 0u;
+      oo[k] = 0;
+      if (e < e1) {
+        int64_t oa, ob;
+        if (lay == EL_CONTIG) {
+          oa = (q.flags & RF_A_SCALAR) ? 0 : e;
+          ob = (q.flags & RF_B_SCALAR) ? 0 : e;
+          oo[k] = e;
+        } else if (lay == EL_ROW2D) {
+          const int64_t r = row_of(q, e), c = e - r * N;
+          oa = r * q.sa_row + c * q.sa_in;
+          ob = r * q.sb_row + c * q.sb_in;
+          oo[k] = r * q.so_row + c;
+        } else {
+          int64_t rem = e, o = 0;
+          oa = ob = 0;
+          for (int d = x->ndim - 1; d >= 0; --d) {
+            const int64_t sz = x->sizes[d];
+            const int64_t i = rem % sz;
+            rem /= sz;
+            oa += i * x->sa[d];
+            ob += i * x->sb[d];
+            o += i * x->so[d];
+          }
+          oo[k] = o;
+        }
+        ra[k] = ld1_raw(q.a, q.dta, oa);
+        if (hasb) rb[k] = ld1_raw(q.b, q.dtb, ob);
       }
     }
-    const float A = ld1(q.a, q.dta, oa);
-    const float B = hasb ? ld1(q.b, q.dtb, ob) : 0.f;
-    float R = 0.f;
-    ew_apply1(v, A, B, R, p0, p1);
-    st1(q.o, q.dto, oo, R);
+    // then one element at a time, from one copy of the operator switch: the
+    // arrays shift down by one per step (their indices stay constant)
+    const int nk = (int)min((int64_t)K, (e1 - eb + 31) / 32);
+#pragma unroll 1
+    for (int k = 0; k < nk; ++k) {
+      float R = 0.f;
+      ew_apply1(v, cvt1(ra[0], q.dta), hasb ? cvt1(rb[0], q.dtb) : 0.f, R, p0, p1);
+      st1(q.o, q.dto, oo[0], R);
+#pragma unroll
+      for (int j = 0; j + 1 < K; ++j) {
+        ra[j] = ra[j + 1];
+        rb[j] = rb[j + 1];
+        oo[j] = oo[j + 1];
+      }
+    }
   }
 }
 
@@ -485,6 +516,54 @@ __device__ __forceinline__ bool combine_arrive(const Exec& ex, uint32_t* cnt, ui
 
 // Rows contiguous: a lane group of q.rg lanes sums one row (nseg == 1), or the
 // whole warp sums one segment of a long row (nseg > 1).
+// Sum of the elements [c, c + n) of one row, `stride` lanes apart: lane i of
+// the group adds elements i, i + stride, ...  Raw loads, kRedU of them in
+// flight per lane, converted and added after they are all issued.
+static constexpr int kRedU = 8;
+
+__device__ __forceinline__ void red_span_scalar(const ReqView& q, int64_t base, int64_t c,
+                                                int64_t c1, int stride, float& acc0,
+                                                float& acc1) {
+#pragma unroll 1
+  for (; c < c1; c += (int64_t)stride * kRedU) {
+    uint32_t w[kRedU];
+#pragma unroll
+    for (int u = 0; u < kRedU; ++u) {
+      w[u] = 0u;
+      if (c + (int64_t)stride * u < c1) w[u] = ld1_raw(q.a, q.dta, base + c + (int64_t)stride * u);
+    }
+#pragma unroll
+    for (int u = 0; u < kRedU; ++u)
+      if (c + (int64_t)stride * u < c1) (u & 1 ? acc1 : acc0) += cvt1(w[u], q.dta);
+  }
+}
+
+// The same over groups of 4 aligned elements: lane i of the group adds groups
+// starting at c + 4 i, c + 4 (i + stride), ... up to c4 (a multiple of 4
+// elements past c); kRedU / 2 groups in flight per lane.
+__device__ __forceinline__ void red_span_vec(const ReqView& q, int64_t base, int64_t c, int64_t c4,
+                                             int stride, float& acc0, float& acc1) {
+  constexpr int U = kRedU / 2;
+#pragma unroll 1
+  for (; c < c4; c += 4 * (int64_t)stride * U) {
+    uint4 w[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      w[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (c + 4 * (int64_t)stride * u < c4) w[u] = ld4_raw(q.a, q.dta, base + c + 4 * (int64_t)stride * u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (c + 4 * (int64_t)stride * u < c4) {
+        float v[4];
+        cvt4(w[u], q.dta, v);
+        acc0 += v[0] + v[2];
+        acc1 += v[1] + v[3];
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool mean, uint32_t k) {
   const int lane = ex.lane;
   const int64_t C = q.inner;
@@ -503,29 +582,11 @@ __device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool 
       if (valid) {
         const int64_t base = r * q.sa_row;
         if (vec) {
-          const int64_t C8 = C & ~(int64_t)7;
-          int64_t c = 8 * li;
-          for (; c + 8 * G < C8; c += 16 * G) {
-            float x[8], y[8];
-            ld8(q.a, q.dta, base + c, x);
-            ld8(q.a, q.dta, base + c + 8 * G, y);
-#pragma unroll
-            for (int t = 0; t < 8; ++t) { acc0 += x[t]; acc1 += y[t]; }
-          }
-          if (c < C8) {
-            float x[8];
-            ld8(q.a, q.dta, base + c, x);
-#pragma unroll
-            for (int t = 0; t < 8; ++t) acc0 += x[t];
-          }
-          for (int64_t t = C8 + li; t < C; t += G) acc1 += ld1(q.a, q.dta, base + t);
+          const int64_t C4 = C & ~(int64_t)3;
+          red_span_vec(q, base, 4 * (int64_t)li, C4, G, acc0, acc1);
+          red_span_scalar(q, base, C4 + li, C, G, acc0, acc1);
         } else {
-          int64_t c = li;
-          for (; c + G < C; c += 2 * G) {
-            acc0 += ld1(q.a, q.dta, base + c);
-            acc1 += ld1(q.a, q.dta, base + c + G);
-          }
-          if (c < C) acc0 += ld1(q.a, q.dta, base + c);
+          red_span_scalar(q, base, li, C, G, acc0, acc1);
         }
       }
       float acc = acc0 + acc1;
@@ -544,24 +605,11 @@ __device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool 
   const int64_t base = r * q.sa_row;
   float acc0 = 0.f, acc1 = 0.f;
   if (vec) {  // c0 is a multiple of 8 (chunk is), c1 may end ragged on the last segment
-    const int64_t c8 = c0 + ((c1 - c0) & ~(int64_t)7);
-    int64_t c = c0 + 8 * lane;
-    for (; c + 256 < c8; c += 512) {
-      float x[8], y[8];
-      ld8(q.a, q.dta, base + c, x);
-      ld8(q.a, q.dta, base + c + 256, y);
-#pragma unroll
-      for (int t = 0; t < 8; ++t) { acc0 += x[t]; acc1 += y[t]; }
-    }
-    if (c < c8) {
-      float x[8];
-      ld8(q.a, q.dta, base + c, x);
-#pragma unroll
-      for (int t = 0; t < 8; ++t) acc0 += x[t];
-    }
-    for (int64_t t = c8 + lane; t < c1; t += 32) acc1 += ld1(q.a, q.dta, base + t);
+    const int64_t c4 = c0 + ((c1 - c0) & ~(int64_t)3);
+    red_span_vec(q, base, c0 + 4 * lane, c4, 32, acc0, acc1);
+    red_span_scalar(q, base, c4 + lane, c1, 32, acc0, acc1);
   } else {
-    for (int64_t c = c0 + lane; c < c1; c += 32) acc0 += ld1(q.a, q.dta, base + c);
+    red_span_scalar(q, base, c0 + lane, c1, 32, acc0, acc1);
   }
   float acc = acc0 + acc1;
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(GPUOS_FULL, acc, off);
@@ -580,7 +628,8 @@ __device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool 
 }
 
 // Rows adjacent in memory (a transposed view): lanes own rows, so every step
-// of the column loop reads rg adjacent rows of cl columns.
+// of the column loop reads rg adjacent rows of cl columns; kRedU columns per
+// lane are in flight (raw loads, converted after all are issued).
 __device__ __forceinline__ void red_cols(const Exec& ex, const ReqView& q, bool mean, uint32_t k) {
   const int lane = ex.lane;
   const int64_t C = q.inner, R = q.numel;
@@ -598,15 +647,18 @@ __device__ __forceinline__ void red_cols(const Exec& ex, const ReqView& q, bool 
   if (valid) {
     const int64_t rb = r * q.sa_row;
     const int64_t sc = q.sa_in;
-    int64_t c = c0 + ci;
-    for (; c + 3 * cl < c1; c += 4 * cl) {
-      const float x0 = ld1(q.a, q.dta, rb + c * sc);
-      const float x1 = ld1(q.a, q.dta, rb + (c + cl) * sc);
-      const float x2 = ld1(q.a, q.dta, rb + (c + 2 * cl) * sc);
-      const float x3 = ld1(q.a, q.dta, rb + (c + 3 * cl) * sc);
-      acc0 += x0; acc1 += x1; acc0 += x2; acc1 += x3;
+#pragma unroll 1
+    for (int64_t c = c0 + ci; c < c1; c += (int64_t)cl * kRedU) {
+      uint32_t w[kRedU];
+#pragma unroll
+      for (int u = 0; u < kRedU; ++u) {
+        w[u] = 0u;
+        if (c + (int64_t)cl * u < c1) w[u] = ld1_raw(q.a, q.dta, rb + (c + (int64_t)cl * u) * sc);
+      }
+#pragma unroll
+      for (int u = 0; u < kRedU; ++u)
+        if (c + (int64_t)cl * u < c1) (u & 1 ? acc1 : acc0) += cvt1(w[u], q.dta);
     }
-    for (; c < c1; c += cl) acc0 += ld1(q.a, q.dta, rb + c * sc);
   }
   float acc = acc0 + acc1;
   for (int off = rg; off < 32; off <<= 1) acc += __shfl_xor_sync(GPUOS_FULL, acc, off);

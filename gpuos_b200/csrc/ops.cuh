@@ -137,32 +137,48 @@ __device__ __forceinline__ void st1(uint64_t base, int dt, int64_t off, float v)
   else reinterpret_cast<__nv_bfloat16*>(base)[off] = __float2bfloat16(v);
 }
 
-// ---- 8-element vector load / store: element offset `e` is a multiple of 8 and
-// the address is 16-byte aligned (checked on the host before RF_VEC is set).
+// ---- raw loads: the bits of 4 (or 1) elements, with nothing computed from
+// them, so that every load of a round is issued before the first one is
+// waited on (a conversion right after each load would wait a full memory
+// round trip per load); cvt4 / cvt1 turn the bits into floats where they are
+// used.  A 16-bit type fills the low two words (or the low 16 bits).
+__device__ __forceinline__ uint4 ld4_raw(uint64_t base, int dt, int64_t e) {
+  if (dt == kF32) return *reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(base) + e);
+  const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(base) + e);
+  return make_uint4(u.x, u.y, 0u, 0u);
+}
+
+__device__ __forceinline__ uint32_t ld1_raw(uint64_t base, int dt, int64_t off) {
+  if (dt == kF32) return reinterpret_cast<const uint32_t*>(base)[off];
+  return reinterpret_cast<const uint16_t*>(base)[off];
+}
+
+__device__ __forceinline__ float cvt1(uint32_t r, int dt) {
+  if (dt == kF32) return __uint_as_float(r);
+  if (dt == kF16) return __half2float(__ushort_as_half((unsigned short)r));
+  return __uint_as_float(r << 16);
+}
+
+__device__ __forceinline__ void bf2_to_f(uint32_t u, float& lo, float& hi);
+
+__device__ __forceinline__ void cvt4(uint4 r, int dt, float* v) {
+  if (dt == kF32) {
+    v[0] = __uint_as_float(r.x); v[1] = __uint_as_float(r.y);
+    v[2] = __uint_as_float(r.z); v[3] = __uint_as_float(r.w);
+  } else if (dt == kF16) {
+    float2 f = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+    v[0] = f.x; v[1] = f.y;
+    f = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    v[2] = f.x; v[3] = f.y;
+  } else {
+    bf2_to_f(r.x, v[0], v[1]);
+    bf2_to_f(r.y, v[2], v[3]);
+  }
+}
+
 __device__ __forceinline__ void bf2_to_f(uint32_t u, float& lo, float& hi) {
   lo = __uint_as_float(u << 16);
   hi = __uint_as_float(u & 0xffff0000u);
-}
-
-__device__ __forceinline__ void ld8(uint64_t base, int dt, int64_t e, float* v) {
-  if (dt == kF32) {
-    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + e);
-    float4 x = p[0], y = p[1];
-    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-    v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
-  } else {
-    uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + e);
-    if (dt == kF16) {
-      float2 f;
-      f = __half22float2(*reinterpret_cast<const __half2*>(&u.x)); v[0] = f.x; v[1] = f.y;
-      f = __half22float2(*reinterpret_cast<const __half2*>(&u.y)); v[2] = f.x; v[3] = f.y;
-      f = __half22float2(*reinterpret_cast<const __half2*>(&u.z)); v[4] = f.x; v[5] = f.y;
-      f = __half22float2(*reinterpret_cast<const __half2*>(&u.w)); v[6] = f.x; v[7] = f.y;
-    } else {
-      bf2_to_f(u.x, v[0], v[1]); bf2_to_f(u.y, v[2], v[3]);
-      bf2_to_f(u.z, v[4], v[5]); bf2_to_f(u.w, v[6], v[7]);
-    }
-  }
 }
 
 // 4-element vector load / store: `e` is a multiple of 4 and the address is
@@ -211,24 +227,6 @@ __device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
 __device__ __forceinline__ uint32_t f2_to_bf2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
-}
-
-__device__ __forceinline__ void st8(uint64_t base, int dt, int64_t e, const float* v) {
-  if (dt == kF32) {
-    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(base) + e);
-    p[0] = make_float4(v[0], v[1], v[2], v[3]);
-    p[1] = make_float4(v[4], v[5], v[6], v[7]);
-  } else {
-    uint4 u;
-    if (dt == kF16) {
-      u.x = f2_to_h2(v[0], v[1]); u.y = f2_to_h2(v[2], v[3]);
-      u.z = f2_to_h2(v[4], v[5]); u.w = f2_to_h2(v[6], v[7]);
-    } else {
-      u.x = f2_to_bf2(v[0], v[1]); u.y = f2_to_bf2(v[2], v[3]);
-      u.z = f2_to_bf2(v[4], v[5]); u.w = f2_to_bf2(v[6], v[7]);
-    }
-    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(base) + e) = u;
-  }
 }
 
 }  // namespace gpuos
