@@ -927,10 +927,19 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       after_prev = lz;
     }
   }
+  // Time per element of a request's chunks relative to a light operator's
+  // fp32 vector chunk: the operator's weight, times 2 for the vector body
+  // with per-row operands and 4 for the general body (from per-chunk timings).
+  auto ew_cost = [](const Pending& p, int v) -> uint64_t {
+    uint64_t w = (uint64_t)chunk_weight(v);
+    if (!(p.r.flags & RF_VEC) || p.r.layout == EL_STRIDED) w *= 4;
+    else if (p.r.layout == EL_ROW2D) w *= 2;
+    return w;
+  };
   // Elementwise chunk size for this batch: about two light-operator chunks'
   // worth of work per resident warp (multiple of 512 elements, 512..8192),
-  // counting each element at its operator's chunk weight; an operator's
-  // chunks get 1/weight of that (at least 128 elements).
+  // counting each element at its cost; a request's chunks get 1/cost of that
+  // (at least 128 elements).
   std::vector<int> var(n);
   uint64_t ew_work = 0;
   for (uint32_t r = 0; r < n; ++r) {
@@ -942,7 +951,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       v = (phys >= 0 && phys < kMaxSlots) ? tab_.slot[phys].variant : V_NONE;
     }
     var[r] = v;
-    if (p.r.kind == RK_EW) ew_work += (uint64_t)p.r.numel * (uint64_t)chunk_weight(v);
+    if (p.r.kind == RK_EW) ew_work += (uint64_t)p.r.numel * ew_cost(p, v);
   }
   const uint64_t warps = (uint64_t)std::max(1, total_warps_);
   uint64_t ce = align_up(std::max<uint64_t>(1, ew_work / (2 * warps)), 512);
@@ -951,7 +960,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     Pending& p = reqs[i + r];
     const int v = var[r];
     if (p.r.kind != RK_EW) continue;
-    uint64_t c = std::max<uint64_t>(128, ce / (uint64_t)chunk_weight(v));
+    uint64_t c = std::max<uint64_t>(128, ce / ew_cost(p, v));
     if (p.r.layout == EL_STRIDED) c = std::min<uint64_t>(c, 2048);
     // equal chunks (a multiple of 4 elements, as the vector path needs)
     const uint64_t numel = (uint64_t)p.r.numel;
