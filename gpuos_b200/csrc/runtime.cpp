@@ -941,6 +941,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   // counting each element at its cost; a request's chunks get 1/cost of that
   // (at least 128 elements).
   std::vector<int> var(n);
+  std::vector<uint8_t> cost_log2(n);  // every cost is a power of two
   uint64_t ew_work = 0;
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + r];
@@ -951,16 +952,19 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       v = (phys >= 0 && phys < kMaxSlots) ? tab_.slot[phys].variant : V_NONE;
     }
     var[r] = v;
-    if (p.r.kind == RK_EW) ew_work += (uint64_t)p.r.numel * ew_cost(p, v);
+    if (p.r.kind == RK_EW) {
+      const uint64_t w = ew_cost(p, v);
+      cost_log2[r] = (uint8_t)__builtin_ctzll(w);
+      ew_work += (uint64_t)p.r.numel << cost_log2[r];
+    }
   }
   const uint64_t warps = (uint64_t)std::max(1, total_warps_);
   uint64_t ce = align_up(std::max<uint64_t>(1, ew_work / (2 * warps)), 512);
   ce = std::min<uint64_t>(std::max<uint64_t>(ce, 512), 8192);
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + r];
-    const int v = var[r];
     if (p.r.kind != RK_EW) continue;
-    uint64_t c = std::max<uint64_t>(128, ce / ew_cost(p, v));
+    uint64_t c = std::max<uint64_t>(128, ce >> cost_log2[r]);
     if (p.r.layout == EL_STRIDED) c = std::min<uint64_t>(c, 2048);
     // equal chunks (a multiple of 4 elements, as the vector path needs)
     const uint64_t numel = (uint64_t)p.r.numel;
@@ -1074,13 +1078,16 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   }
   std::memcpy(cbp, cb.data(), 4ull * (n + 1));
   {
+    // granule j starts at chunk j * gran, inside the request whose chunks
+    // [cb[r], cb[r + 1]) hold it: walk the requests once
     uint32_t* gt = reinterpret_cast<uint32_t*>(base + gtab_off);
-    uint32_t r = 0;
-    for (uint64_t j = 0; j < ngran; ++j) {
-      const uint64_t c = j * gran;
-      while (r + 1 < n && cb[r + 1] <= c) ++r;
-      gt[2 * j] = r;
-      gt[2 * j + 1] = cb[r];
+    uint64_t j = 0;
+    for (uint32_t r = 0; r < n && j < ngran; ++r) {
+      const uint64_t end = cb[r + 1];
+      for (uint64_t c = j * gran; c < end; c = ++j * gran) {
+        gt[2 * j] = r;
+        gt[2 * j + 1] = cb[r];
+      }
     }
   }
   if (staged) {
