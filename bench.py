@@ -337,6 +337,74 @@ def cpu_baseline(stream, min_seconds=5.0):
                       f"({el:.1f} s wall, liboracle.so on {used} threads)"}
 
 
+def decode_chain(ext, dev, batches=(1, 8, 64), layers=32, steps=20, warmup=3):
+    """The transformer-decode pointwise chain (bf16), through the public API.
+
+    Per layer: residual add; x*x; mean(-1, keepdim); + 1e-6; pow(-0.5); * rstd
+    ([b,1] broadcast); * weight [4096]; + bias; sigmoid(u) and * u2 on
+    [b,11008].  Ten requests per layer, each but the gate depending on the one
+    before, so one flush of a step runs them in stage order.  A step is all
+    `layers` layers and one flush(sync=True); inputs are N(0, 0.02).
+    Reports requests/s, the host's submit time per request, and the time
+    from the step's flush(sync=True) call to its return (planning, the batch
+    on the GPU in stage order, completion)."""
+    from gpuos_b200 import workloads as W
+    bf = torch.bfloat16
+    H, F = 4096, 11008
+    s_sig = ext.register_elementwise("sigmoid|f32", *W.EXPR["sigmoid"])
+    s_pow = ext.register_elementwise("pow|f32", *W.EXPR["pow"])
+    s_mean = ext.register_reduce("reduce_mean", "mean")
+    out = {}
+    for b in batches:
+        g = torch.Generator(device=dev).manual_seed(b)
+
+        def normal(*shape):
+            return (torch.randn(*shape, generator=g, device=dev) * 0.02).to(bf)
+
+        def empty(*shape):
+            return torch.empty(*shape, dtype=bf, device=dev)
+
+        eps = torch.tensor(1e-6, dtype=bf, device=dev)
+        nhalf = torch.tensor(-0.5, dtype=bf, device=dev)
+        x0 = normal(b, H)
+        L = []
+        for _ in range(layers):
+            L.append(dict(res=normal(b, H), w=normal(H), bias=normal(H), u=normal(b, F),
+                          u2=normal(b, F), h=empty(b, H), sq=empty(b, H), ms=empty(b, 1),
+                          mse=empty(b, 1), rstd=empty(b, 1), hn=empty(b, H), hw=empty(b, H),
+                          xo=empty(b, H), gt=empty(b, F), act=empty(b, F)))
+        sub_s, fl_s, wall_s = 0.0, 0.0, 0.0
+        for it in range(warmup + steps):
+            t0 = time.perf_counter()
+            x = x0
+            for l in L:
+                ext.submit_add(x, l["res"], l["h"])
+                ext.submit_mul(l["h"], l["h"], l["sq"])
+                ext.submit_reduce(s_mean, l["sq"], l["ms"], [1], True)
+                ext.submit_add(l["ms"], eps, l["mse"])
+                ext.submit_binary(s_pow, l["mse"], nhalf, l["rstd"])
+                ext.submit_mul(l["h"], l["rstd"], l["hn"])
+                ext.submit_mul(l["hn"], l["w"], l["hw"])
+                ext.submit_add(l["hw"], l["bias"], l["xo"])
+                ext.submit_unary(s_sig, l["u"], l["gt"])
+                ext.submit_mul(l["gt"], l["u2"], l["act"])
+                x = l["xo"]
+            t1 = time.perf_counter()
+            ext.flush(sync=True)
+            t2 = time.perf_counter()
+            if it >= warmup:
+                sub_s += t1 - t0
+                fl_s += t2 - t1
+                wall_s += t2 - t0
+        n = 10 * layers * steps
+        out[f"b{b}"] = {"requests_per_step": 10 * layers,
+                        "requests_per_s": round(n / wall_s, 1),
+                        "host_submit_ns_per_request": round(sub_s / n * 1e9, 1),
+                        "flush_sync_us_per_step": round(fl_s / steps * 1e6, 1),
+                        "flush_sync_ns_per_request": round(fl_s / n * 1e9, 1)}
+    return out
+
+
 def flush_latency(ext, dev, reps=400):
     """p50 of flush(sync=True) for one 4096-element add, and for the
     1024 x 4096 add/mul batch."""
@@ -519,6 +587,7 @@ def bench_ours(args, world, rank, local):
     e2e.check(stream, dout)
 
     lat = flush_latency(ext, dev) if rank == 0 else None
+    chain = decode_chain(ext, dev) if rank == 0 else None
     ext.shutdown()
 
     peak, peak_kind = peaks()
@@ -558,6 +627,7 @@ def bench_ours(args, world, rank, local):
         "roofline": roof,
         "cpu_baseline": cpu,
         "flush_p50_us": lat,
+        "decode_chain": chain,
         "gpu_launches": int(launches * world),
         "clocks": clk,
     }

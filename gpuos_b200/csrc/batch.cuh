@@ -159,9 +159,14 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
         if (w > waited) {
           // every chunk of the earlier stages must be done first
           if (lane == 0 && ld_acquire_u32(&ex.st->done) < w) {
+            // exponential back-off: thousands of warps may wait on this one
+            // counter, and their polls would queue the increments of the
+            // chunks they wait for
             const uint64_t t0 = globaltimer();
+            unsigned ns = 64;
             while (ld_acquire_u32(&ex.st->done) < w) {
-              __nanosleep(128);
+              __nanosleep(ns);
+              if (ns < 1024) ns <<= 1;
               if (globaltimer() - t0 > ex.wait_limit_ns) {
                 atomicOr(&ex.st->err, ERR_STAGE_TIMEOUT);
                 break;
