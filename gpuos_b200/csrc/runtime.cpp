@@ -961,10 +961,25 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   const uint64_t warps = (uint64_t)std::max(1, total_warps_);
   uint64_t ce = align_up(std::max<uint64_t>(1, ew_work / (2 * warps)), 512);
   ce = std::min<uint64_t>(std::max<uint64_t>(ce, 512), 8192);
+  // A batch with stage barriers runs its stages one after another, each on
+  // as many warps as it has chunks: a stage's chunks are sized from its own
+  // work spread over every warp (one chunk per granule, below), not from the
+  // whole batch's.
+  std::vector<uint64_t> stage_ce;
+  if (staged) {
+    std::vector<uint64_t> sw(n, 0);
+    for (uint32_t r = 0; r < n; ++r)
+      if (reqs[i + r].r.kind == RK_EW) sw[stage_first[r]] += (uint64_t)reqs[i + r].r.numel << cost_log2[r];
+    stage_ce.resize(n);
+    for (uint32_t r = 0; r < n; ++r) {
+      const uint64_t c = align_up(std::max<uint64_t>(1, sw[stage_first[r]] / warps), 128);
+      stage_ce[r] = std::min<uint64_t>(std::max<uint64_t>(c, 512), 8192);
+    }
+  }
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + r];
     if (p.r.kind != RK_EW) continue;
-    uint64_t c = std::max<uint64_t>(128, ce >> cost_log2[r]);
+    uint64_t c = std::max<uint64_t>(128, (staged ? stage_ce[r] : ce) >> cost_log2[r]);
     if (p.r.layout == EL_STRIDED) c = std::min<uint64_t>(c, 2048);
     // equal chunks (a multiple of 4 elements, as the vector path needs)
     const uint64_t numel = (uint64_t)p.r.numel;
@@ -1008,8 +1023,10 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   if (nchunk > 0xffffffffull) throw GError(GPUOS_EINVAL, "batch too large");
   // Granules: the unit of work a warp takes at a time, about two per warp
   // (at most 8 chunks each).
+  // (a batch with stage barriers: one chunk each, so that a stage spreads
+  // over as many warps as it has chunks)
   const uint64_t warps_all = (uint64_t)std::max(1, total_warps_);
-  uint64_t gran = nchunk / (2 * warps_all);
+  uint64_t gran = staged ? 1 : nchunk / (2 * warps_all);
   gran = std::min<uint64_t>(std::max<uint64_t>(gran, 1), 8);
   const uint64_t ngran = (nchunk + gran - 1) / gran;
   const uint64_t rec_off = sizeof(BatchHdr);
