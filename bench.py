@@ -233,6 +233,15 @@ def barrier(world):
 
 
 # ---------------------------------------------------------------------------
+def workload_desc(name, stream):
+    """The workload as both arms of the bench name it in `config`."""
+    m = stream.meta
+    if name == "mixed_24op":
+        return (f"{name}: {len(stream.requests)} requests, {m['ops']} ops, {m['dtype']}, sizes "
+                f"log-uniform [{m['sizes'][0]}, {m['sizes'][1]}], flush every {stream.flush_every}")
+    return f"{name}: {len(stream.requests)} requests, flush every {stream.flush_every}"
+
+
 def make_stream(name):
     from gpuos_b200 import workloads as W
     return W.STREAMS[name]()
@@ -616,8 +625,7 @@ def bench_ours(args, world, rank, local):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seed 0)",
-        "config": {"workload": f"{args.workload}: {n_req} requests, 24 ops, fp32, sizes "
-                               "log-uniform [256, 32768], flush every 512",
+        "config": {"workload": workload_desc(args.workload, stream),
                    "mode": args.mode, "api": "gpuos_ext.submit_* per request",
                    "l2": f"inputs {stream.in_bytes / 1e9:.2f} GB per step > 126 MB L2",
                    "parallelism": f"{world} independent executors (one per GPU)"},
@@ -660,7 +668,7 @@ def bench_reference(args, world, rank):
         "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seed 0)",
-        "config": {"workload": f"{args.workload}: {len(stream.requests)} requests",
+        "config": {"workload": workload_desc(args.workload, stream),
                    "engine": "liboracle.so (C port of the reference algorithm), all host cores"},
         "cpu_baseline": {"value": round(v, 1), "unit": "requests/s", "cores": used, "kind": "port",
                          "sample": f"the whole stream, {args.steps} steps"},
