@@ -24,9 +24,12 @@ receives the result (scheduler.py:118, 157-160, 349-358).  Chains need no
 fusion for correctness here: the executor orders a request after the earlier
 requests of the flush whose outputs it reads.
 
-An op that is not scheduled and reads a pending output, or writes a tensor a
-pending request reads or writes, forces a synchronous flush first (the
-reference checks reads of outputs only, scheduler.py:55-99).  Tensors larger than ``size_threshold``
+An op that is not scheduled and reads memory a pending request writes, or
+writes memory a pending request reads or writes, forces a synchronous flush
+first.  Pending requests are tracked by the byte ranges of their tensors in
+their storages, so a slice, a transpose or any other view of a pending
+tensor counts (the reference compares data_ptr values of pending outputs
+only, scheduler.py:55-99, which misses views that start elsewhere).  Tensors larger than ``size_threshold``
 elements, ops under autograd, CPU tensors, and ``add``/``sub`` with
 ``alpha != 1`` (which the reference ignores) run in torch.
 """
@@ -35,7 +38,7 @@ from __future__ import annotations
 import contextlib
 import os
 import threading
-from typing import Any, Optional, Set
+from typing import Any, Dict, List, Optional, Set, Tuple
 
 import torch
 
@@ -121,6 +124,36 @@ def _param_expr(name: str, args, kwargs) -> Optional[tuple]:
     return None
 
 
+def _extent(t: torch.Tensor) -> Optional[Tuple[int, int, int]]:
+    """(storage address, first byte, one past the last byte) a tensor view
+    covers in its storage, or None for an empty tensor."""
+    if t.numel() == 0:
+        return None
+    lo = hi = t.storage_offset()
+    for n, st in zip(t.shape, t.stride()):
+        if n > 1:
+            if st >= 0:
+                hi += (n - 1) * st
+            else:
+                lo += (n - 1) * st
+    es = t.element_size()
+    return t.untyped_storage().data_ptr(), lo * es, (hi + 1) * es
+
+
+def _overlaps(e, table) -> bool:
+    if e is None:
+        return False
+    for lo, hi in table.get(e[0], ()):
+        if e[1] < hi and lo < e[2]:
+            return True
+    return False
+
+
+def _add(e, table):
+    if e is not None:
+        table.setdefault(e[0], []).append((e[1], e[2]))
+
+
 class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
     def __init__(self, ext, *, size_threshold: int, auto_flush_ms: Optional[float],
                  pending: Set[int], jit: bool):
@@ -130,6 +163,9 @@ class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
         self.auto_flush_ms = auto_flush_ms
         self.pending = pending  # data_ptr of every output not yet flushed synchronously
         self.pending_in: Set[int] = set()  # data_ptr of their inputs
+        # byte ranges the pending requests write / read, per storage
+        self._w: Dict[int, List[Tuple[int, int]]] = {}
+        self._r: Dict[int, List[Tuple[int, int]]] = {}
         self.jit = jit
         self._names = _scheduled_names(jit)
         self._stop = threading.Event()
@@ -161,9 +197,11 @@ class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
         return True
 
     def _reads_pending(self, args, kwargs) -> bool:
+        """Does any CUDA tensor among the arguments overlap what a pending
+        request writes?"""
         def walk(o: Any) -> bool:
             if isinstance(o, torch.Tensor):
-                return o.is_cuda and o.data_ptr() in self.pending
+                return o.is_cuda and _overlaps(_extent(o), self._w)
             if isinstance(o, (list, tuple)):
                 return any(walk(i) for i in o)
             if isinstance(o, dict):
@@ -172,21 +210,31 @@ class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
         return walk(args) or walk(kwargs)
 
     def _writes_pending(self, func, args, kwargs) -> bool:
-        busy = self.pending | self.pending_in
+        """Does the op write memory a pending request reads or writes?"""
         for i, a in enumerate(func._schema.arguments):
             v = kwargs.get(a.name) if a.kwarg_only or i >= len(args) else args[i]
             if a.alias_info is not None and a.alias_info.is_write:
                 ts = v if isinstance(v, (list, tuple)) else [v]
                 for t in ts:
-                    if isinstance(t, torch.Tensor) and t.is_cuda and t.data_ptr() in busy:
-                        return True
+                    if isinstance(t, torch.Tensor) and t.is_cuda:
+                        e = _extent(t)
+                        if _overlaps(e, self._w) or _overlaps(e, self._r):
+                            return True
         return False
 
     def _done(self, out: torch.Tensor, *inputs) -> torch.Tensor:
         self.pending.add(out.data_ptr())
+        _add(_extent(out), self._w)
         for t in inputs:
             self.pending_in.add(t.data_ptr())
+            _add(_extent(t), self._r)
         return out
+
+    def clear_pending(self):
+        self.pending.clear()
+        self.pending_in.clear()
+        self._w.clear()
+        self._r.clear()
 
     def _out_for(self, kwargs, shape, dtype, device) -> Optional[torch.Tensor]:
         out = kwargs.get("out")
@@ -208,8 +256,7 @@ class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
         if self.pending and (self._reads_pending(args, kwargs) or
                              self._writes_pending(func, args, kwargs)):
             self.ext.flush(sync=True)
-            self.pending.clear()
-            self.pending_in.clear()
+            self.clear_pending()
         return func(*args, **kwargs)
 
     def _schedule(self, name, func, args, kwargs):
@@ -307,7 +354,7 @@ class GPUOSScheduler:
         if sync:
             self._pending.clear()
             if self._mode is not None:
-                self._mode.pending_in.clear()
+                self._mode.clear_pending()
 
     def __exit__(self, exc_type, exc, tb):
         try:

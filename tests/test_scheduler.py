@@ -167,6 +167,53 @@ def test_write_after_read_is_ordered(monkeypatch):
     assert torch.equal(ga.cpu(), a * 3.0)
 
 
+def test_pending_extents_cover_views():
+    """The byte ranges the scheduler tracks: a slice, a transposed view or a
+    narrowed view of a tensor overlaps it; a disjoint slice of the same
+    storage does not, nor does another tensor."""
+    x = torch.zeros(8, 16)
+    table = {}
+    S._add(S._extent(x[2:4]), table)
+    assert S._overlaps(S._extent(x), table)
+    assert S._overlaps(S._extent(x[3]), table)
+    assert S._overlaps(S._extent(x.t()[5]), table)        # column 5 crosses rows 2..3
+    assert S._overlaps(S._extent(x.narrow(0, 3, 5)), table)
+    assert not S._overlaps(S._extent(x[4:]), table)
+    assert not S._overlaps(S._extent(x[:2]), table)
+    assert not S._overlaps(S._extent(torch.zeros(8, 16)), table)
+    assert S._extent(torch.zeros(0)) is None
+
+
+@pytest.mark.gpu
+def test_torch_op_on_a_view_of_a_pending_output_waits(monkeypatch):
+    """Reading out[1:] (another data_ptr than out) of a scheduled add before
+    any flush sees the add's result."""
+    monkeypatch.delenv("GPUOS_SCHEDULER_DISABLE_JIT", raising=False)
+    g = torch.Generator().manual_seed(56)
+    a, b = torch.randn(3000, generator=g), torch.randn(3000, generator=g)
+    ga, gb = a.to(DEV), b.to(DEV)
+    with torch.no_grad(), S.scheduler_context(auto_flush_ms=None):
+        c = ga + gb
+        tail = c[1:].clone()          # aten::clone of a view: runs in torch
+        col = (c.view(30, 100).t()[7]).clone()
+    want = _exact(a, b, "add")
+    assert torch.equal(tail.cpu(), want[1:])
+    assert torch.equal(col.cpu(), want.view(30, 100).t()[7])
+
+
+@pytest.mark.gpu
+def test_torch_write_into_a_view_of_a_pending_input_waits(monkeypatch):
+    monkeypatch.delenv("GPUOS_SCHEDULER_DISABLE_JIT", raising=False)
+    g = torch.Generator().manual_seed(57)
+    a, b = torch.randn(3000, generator=g), torch.randn(3000, generator=g)
+    ga, gb = a.to(DEV), b.to(DEV)
+    with torch.no_grad(), S.scheduler_context(auto_flush_ms=None):
+        c = ga * gb
+        ga[5:].zero_()                # writes a view of the pending mul's input
+    assert torch.equal(c.cpu(), _exact(a, b, "mul"))
+    assert float(ga[5:].abs().sum()) == 0.0
+
+
 @pytest.mark.gpu
 def test_large_tensors_and_autograd_stay_in_torch(monkeypatch):
     monkeypatch.delenv("GPUOS_SCHEDULER_DISABLE_JIT", raising=False)
