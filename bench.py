@@ -471,10 +471,8 @@ def roofline_leg(stream, dev, steps, peak_gbs, peak_kind):
         # the same routing as the Python API, bound to this executor
         sub = W.Submitter(_CabiExt(ex))
         calls = sub.prepare(stream, views)
-        batch_bytes = []
-        for i in range(0, len(stream.requests), fe):
-            batch_bytes.append(sum(r.algo_bytes for r in stream.requests[i:i + fe]))
-        per = len(batch_bytes)
+        step_bytes = sum(r.algo_bytes for r in stream.requests)
+        per = None  # launches per step, counted from the executor
         cur = torch.cuda.current_stream()
         cs = cur.cuda_stream
         region_s, launches = 0.0, 0
@@ -490,7 +488,8 @@ def roofline_leg(stream, dev, steps, peak_gbs, peak_kind):
             e1.record(cur)
             n = ex.stats()["published"] - q0
             ex.flush(sync=True, stream=cs)
-            assert n == per, (n, per)
+            assert per is None or n == per, (n, per)
+            per = n
             if s >= 1:
                 region_s += e0.elapsed_time(e1) / 1e3
                 launches += n
@@ -506,14 +505,15 @@ def roofline_leg(stream, dev, steps, peak_gbs, peak_kind):
             ex.flush(sync=True, stream=cs)
         ms = ex.take_timings()
         assert len(ms) == steps * per, (len(ms), steps, per)
-        tot_bytes = sum(batch_bytes) * steps
+        lean = ex.stats()["lean"] > 0
+        tot_bytes = step_bytes * steps
         achieved = tot_bytes / region_s / 1e9
         return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs,
                 "unit": "GB/s", "frac": round(achieved / peak_gbs, 4), "peak_kind": peak_kind,
-                "kernel": "gpuos_batch_kernel",
+                "kernel": "gpuos_lean_kernel" if lean else "gpuos_batch_kernel",
                 "avg_launch_us": round(region_s / launches * 1e6, 2),
                 "per_launch_event_us": round(sum(ms) / len(ms) * 1e3, 2),
-                "bytes_per_launch": int(sum(batch_bytes) / per),
+                "bytes_per_launch": int(step_bytes / per),
                 "launches": launches, "traffic": None}
     finally:
         ex.close()

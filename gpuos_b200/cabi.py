@@ -28,13 +28,14 @@ class Options(ctypes.Structure):
     _fields_ = [("capacity", ctypes.c_int32), ("threads_per_block", ctypes.c_int32),
                 ("mode", ctypes.c_int32), ("blocks_per_sm", ctypes.c_int32),
                 ("idle_ms", ctypes.c_double), ("sync_timeout_s", ctypes.c_double),
-                ("max_batch", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7)]
+                ("max_batch", ctypes.c_int32), ("wait_limit_us", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 6)]
 
 
 class Stats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in (
         "published", "staged", "processed", "retired", "heartbeat", "requests", "pending",
-        "errors", "relaunches", "dev_ns")] + [(n, ctypes.c_int32) for n in (
+        "errors", "relaunches", "dev_ns", "lean")] + [(n, ctypes.c_int32) for n in (
             "capacity", "max_batch", "mode", "worker_alive", "quit", "grid", "block", "device")]
 
 
@@ -76,6 +77,7 @@ SIGNATURES = {
     "gpuos_set_yield_every": (ctypes.c_int32, [_VP, ctypes.c_uint64]),
     "gpuos_set_debug_level": (ctypes.c_int32, [_VP, ctypes.c_int32]),
     "gpuos_worker_alive": (ctypes.c_int32, [_VP]),
+    "gpuos_debug_stall_next_batch": (ctypes.c_int32, [_VP]),
     "gpuos_plan_elementwise": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_float, ctypes.c_float,
                                                 P(Tensor), P(Tensor), P(Tensor), P(Plan)]),
     "gpuos_plan_reduce": (ctypes.c_int32, [ctypes.c_int32, P(Tensor), P(Tensor), P(ctypes.c_int32),
@@ -182,10 +184,11 @@ class Executor:
     """Thin owner of one gpuos_executor handle."""
 
     def __init__(self, device=0, mode=MODE_PERSISTENT, capacity=4096, threads_per_block=256,
-                 max_batch=0, idle_ms=0.0):
+                 max_batch=0, idle_ms=0.0, wait_limit_us=0, sync_timeout_s=0.0):
         o = Options()
         o.capacity, o.threads_per_block, o.mode = capacity, threads_per_block, mode
         o.max_batch, o.idle_ms = max_batch, idle_ms
+        o.wait_limit_us, o.sync_timeout_s = wait_limit_us, sync_timeout_s
         h = ctypes.c_void_p()
         check(lib().gpuos_executor_create(device, ctypes.byref(o), ctypes.byref(h)))
         self.h = h
@@ -265,6 +268,11 @@ class Executor:
         n = ctypes.c_uint64()
         check(lib().gpuos_take_timings(self.h, buf, cap, ctypes.byref(n)))
         return list(buf[:min(n.value, cap)])
+
+    def stall_next_batch(self):
+        """Fault injection: the next batch with stage barriers waits for a
+        chunk that never comes, until its bounded wait runs out."""
+        check(lib().gpuos_debug_stall_next_batch(self.h))
 
     def set_yield_every(self, n):
         check(lib().gpuos_set_yield_every(self.h, n))

@@ -286,6 +286,8 @@ PyObject* stats_dict(const gpuos_stats& s, bool reference_keys_only) {
     put("requests", PyLong_FromUnsignedLongLong(s.requests));
     put("errors", PyLong_FromUnsignedLongLong(s.errors));
     put("relaunches", PyLong_FromUnsignedLongLong(s.relaunches));
+    put("dev_ns", PyLong_FromUnsignedLongLong(s.dev_ns));
+    put("lean", PyLong_FromUnsignedLongLong(s.lean));
     put("worker_alive", PyBool_FromLong(s.worker_alive));
     put("grid", PyLong_FromLong(s.grid));
     put("block", PyLong_FromLong(s.block));

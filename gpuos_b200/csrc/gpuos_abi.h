@@ -231,6 +231,50 @@ struct alignas(64) DevCtrl {
   uint32_t ready_off[kDoneRing];
 };
 
+// ---- lean batches --------------------------------------------------------
+// A stream-mode batch whose requests are all contiguous, 16-byte aligned fp32
+// elementwise requests of a precompiled operator with tensor (not scalar)
+// operands (the mixed-operator stream,
+// the add/mul stream) travels entirely in the kernel's parameters: no staging
+// copy, no granule table.  Warp g of W runs the chunks
+// [g * nchunk / W, (g + 1) * nchunk / W), so the warps of one SM work on
+// neighbouring chunks, which the host has grouped by operator.
+static constexpr int kLeanThreads = 1024;   // one CTA per SM
+static constexpr int kLeanPar = 16;         // distinct (p0, p1) pairs per batch
+static constexpr int kLeanMaxReq = 512;     // largest parameter block (about 22 KB)
+
+enum LeanFlags : uint32_t {
+  LEAN_WAIT_FIRST = 1,   // wait for the previous grid in the stream before touching memory
+};
+
+struct alignas(8) LeanRec {
+  uint64_t a, b, o;      // device addresses (b unused without RF_HAS_B)
+  uint32_t numel;        // output elements (< 2^31)
+  uint32_t chunk;        // elements per chunk (a multiple of 4)
+  uint8_t  op;           // precompiled elementwise variant
+  uint8_t  flags;        // RF_HAS_B
+  uint8_t  pidx;         // its (p0, p1) in LeanHdr::par
+  uint8_t  pad[5];
+};
+static_assert(sizeof(LeanRec) == 40, "LeanRec must stay 40 bytes");
+
+struct alignas(16) LeanHdr {
+  uint64_t seq;
+  uint64_t st;           // BatchState* of the batch (device)
+  uint64_t done_ring;    // completion words (device view of mapped host memory)
+  uint32_t nreq, nchunk;
+  uint32_t flags;        // LeanFlags
+  uint32_t pad;
+  float    par[kLeanPar][2];
+};
+
+template <int N>
+struct LeanBatch {
+  LeanHdr  h;
+  uint32_t cb[N + 1];    // first chunk of every request; cb[nreq] = nchunk
+  LeanRec  rec[N];
+};
+
 // Arguments of the persistent worker kernel.
 struct WorkerArgs {
   uint8_t* ring;                 // device staging ring

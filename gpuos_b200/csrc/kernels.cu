@@ -14,8 +14,17 @@
 //
 // Every wait in these kernels is bounded by %globaltimer.
 #include "batch.cuh"
+#include "lean.cuh"
 
 namespace gpuos {
+
+// Lean batches (lean.cuh): the whole batch is the kernel's parameter block,
+// in three sizes so that a small batch does not ship 22 KB of parameters.
+template <int N>
+__global__ void __launch_bounds__(kLeanThreads, 1)
+gpuos_lean_kernel(const __grid_constant__ LeanBatch<N> bt) {
+  lean_batch(bt);
+}
 
 // The batch's descriptors are in the device staging ring (payload); its
 // counters are `st`, one slot of a device array.
@@ -184,6 +193,44 @@ extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, cudaStrea
   const gpuos::WorkerArgs* w = static_cast<const gpuos::WorkerArgs*>(args);
   gpuos::gpuos_worker_kernel<<<grid, gpuos::kCtaThreads, 0, stream>>>(*w);
   return cudaGetLastError();
+}
+
+// Launch a lean batch (`params` points at a LeanBatch<32>, <128> or <512>, by
+// size_class 0, 1, 2) on `grid` CTAs, with programmatic dependent launch.
+extern "C" cudaError_t gpuos_launch_lean(const void* params, int size_class, int grid,
+                                         cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(gpuos::kLeanThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  switch (size_class) {
+    case 0:
+      return cudaLaunchKernelEx(&cfg, gpuos::gpuos_lean_kernel<32>,
+                                *static_cast<const gpuos::LeanBatch<32>*>(params));
+    case 1:
+      return cudaLaunchKernelEx(&cfg, gpuos::gpuos_lean_kernel<128>,
+                                *static_cast<const gpuos::LeanBatch<128>*>(params));
+    case 2:
+      return cudaLaunchKernelEx(&cfg, gpuos::gpuos_lean_kernel<gpuos::kLeanMaxReq>,
+                                *static_cast<const gpuos::LeanBatch<gpuos::kLeanMaxReq>*>(params));
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+extern "C" size_t gpuos_lean_params_size(int size_class) {
+  switch (size_class) {
+    case 0: return sizeof(gpuos::LeanBatch<32>);
+    case 1: return sizeof(gpuos::LeanBatch<128>);
+    case 2: return sizeof(gpuos::LeanBatch<gpuos::kLeanMaxReq>);
+    default: return 0;
+  }
 }
 
 // Resident blocks per SM of the two kernels (the persistent grid must be

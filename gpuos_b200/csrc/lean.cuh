@@ -1,0 +1,172 @@
+// The lean batch kernel: stream-mode batches of contiguous, aligned fp32
+// elementwise requests of the precompiled operators, with the whole batch in
+// the kernel's parameters (struct LeanBatch, gpuos_abi.h).
+//
+// Why it exists: such batches are the mixed-operator and add/mul streams.
+// The general batch kernel carries every body (strided views, per-row
+// operands, 16-bit types, reductions, stage barriers) and needs 128 registers
+// per thread, so an SM holds 16 warps, and neighbouring warps run different
+// operator bodies out of one large kernel: a third of the stall cycles were
+// instruction fetch.  Here:
+//   * one CTA of 1024 threads per SM, 64 registers per thread (32 warps);
+//   * warp g of W runs the contiguous chunk range [g n / W, (g + 1) n / W):
+//     the host sorts a batch's requests by operator, so the warps of an SM
+//     run one or two operator bodies;
+//   * a warp finds its first request by a binary search of the chunk prefix
+//     in parameter space and reads records from there: no staging copy of
+//     the batch, no granule table, no dependent global loads before the
+//     first data load;
+//   * programmatic dependent launch: a batch launches while the previous one
+//     drains.  It waits for the previous grid before touching memory when
+//     the host says so (LEAN_WAIT_FIRST: the first batch of a flush, or a
+//     hazard with an earlier batch of the same flush), lets the next batch
+//     launch once it runs, and waits for the previous grid before it exits,
+//     so that batches complete in stream order.
+//   * completion: the last CTA posts the batch's completion word (seq + 1)
+//     to mapped host memory.
+#pragma once
+#include "executor.cuh"
+
+namespace gpuos {
+
+__device__ __forceinline__ void gdc_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void gdc_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// 4-element groups per lane in flight per round: 4 for the light operators,
+// 2 for those with a division, a square root or a transcendental function.
+template <int V>
+__device__ __forceinline__ constexpr int lean_groups() {
+  return op_unroll<V>() == 2 ? 4 : 2;
+}
+
+struct LeanCur {
+  const float* a;
+  const float* b;
+  float* o;
+  uint32_t numel, chunk;
+  int op, pidx;
+};
+
+// elements [e0, e0 + n) of one request, n > 0 (unary operators ignore b)
+template <int V, int N>
+__device__ __forceinline__ void lean_chunk(const LeanCur& u, const LeanBatch<N>& bt, uint32_t e0,
+                                           uint32_t n, int lane) {
+  constexpr int kG = lean_groups<V>();
+  constexpr bool kBin = V == V_ADD || V == V_MUL || V == V_SUB || V == V_DIV0 || V == V_DIV ||
+                        V == V_MAX || V == V_MIN || V == V_POW;
+  const float p0 = bt.h.par[u.pidx][0], p1 = bt.h.par[u.pidx][1];
+  const uint32_t nq = n >> 2;
+  const float4* A = reinterpret_cast<const float4*>(u.a + e0);
+  const float4* B = reinterpret_cast<const float4*>(u.b + e0);
+  float4* O = reinterpret_cast<float4*>(u.o + e0);
+#pragma unroll 1
+  for (uint32_t q0 = lane; q0 < nq; q0 += 32 * kG) {
+    float4 a[kG], b[kG];
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      a[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+      b[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (q0 + 32 * g < nq) {
+        a[g] = A[q0 + 32 * g];
+        if (kBin) b[g] = B[q0 + 32 * g];
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      if (q0 + 32 * g < nq) {
+        float4 r;
+        r.x = op1<V>(a[g].x, b[g].x, p0, p1);
+        r.y = op1<V>(a[g].y, b[g].y, p0, p1);
+        r.z = op1<V>(a[g].z, b[g].z, p0, p1);
+        r.w = op1<V>(a[g].w, b[g].w, p0, p1);
+        O[q0 + 32 * g] = r;
+      }
+    }
+  }
+  if (lane < (int)(n & 3u)) {
+    const uint32_t e = e0 + 4 * nq + lane;
+    u.o[e] = op1<V>(u.a[e], kBin ? u.b[e] : 0.f, p0, p1);
+  }
+}
+
+#define GPUOS_LEAN_CASE(V) case V: lean_chunk<V>(u, bt, e0, n, lane); return;
+
+template <int N>
+__device__ __forceinline__ void lean_dispatch(const LeanCur& u, const LeanBatch<N>& bt, uint32_t e0,
+                                              uint32_t n, int lane) {
+  switch (u.op) {
+    GPUOS_ALL_EW(GPUOS_LEAN_CASE)
+    default: return;
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void lean_decode(LeanCur& u, const LeanBatch<N>& bt, uint32_t r) {
+  const LeanRec& q = bt.rec[r];
+  u.a = reinterpret_cast<const float*>(q.a);
+  u.b = reinterpret_cast<const float*>(q.b);
+  u.o = reinterpret_cast<float*>(q.o);
+  u.numel = q.numel;
+  u.chunk = q.chunk;
+  u.op = q.op;
+  u.pidx = q.pidx;
+}
+
+template <int N>
+__device__ __forceinline__ void lean_batch(const LeanBatch<N>& bt) {
+  const LeanHdr& h = bt.h;
+  if (h.flags & LEAN_WAIT_FIRST) gdc_wait();
+  gdc_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  constexpr uint32_t kWarps = kLeanThreads / 32;
+  const uint64_t W = (uint64_t)gridDim.x * kWarps;
+  const uint64_t gw = (uint64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const uint32_t nchunk = h.nchunk;
+  const uint32_t c0 = (uint32_t)(gw * nchunk / W);
+  const uint32_t c1 = (uint32_t)((gw + 1) * nchunk / W);
+  if (c0 < c1) {
+    // the request holding chunk c0: cb[lo] <= c0 < cb[lo + 1]
+    uint32_t lo = 0, hi = h.nreq;
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (bt.cb[mid] <= c0) lo = mid;
+      else hi = mid;
+    }
+    uint32_t r = lo;
+    LeanCur u;
+    lean_decode(u, bt, r);
+    uint32_t rbase = bt.cb[r], rend = bt.cb[r + 1];
+    for (uint32_t c = c0; c < c1; ++c) {
+      if (c >= rend) {
+        do {
+          ++r;
+          rbase = rend;
+          rend = bt.cb[r + 1];
+        } while (c >= rend);
+        lean_decode(u, bt, r);
+      }
+      const uint32_t e0 = (c - rbase) * u.chunk;
+      const uint32_t n = min(u.chunk, u.numel - e0);
+      lean_dispatch(u, bt, e0, n, lane);
+    }
+  }
+  // completion: every CTA releases its stores, the last one posts the word
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    BatchState* st = reinterpret_cast<BatchState*>(h.st);
+    const uint32_t left = atomicAdd(&st->ctas_left, 1u) + 1u;
+    if (left == gridDim.x) {
+      __threadfence();
+      st->ctas_left = 0u;
+      volatile uint64_t* dr = reinterpret_cast<volatile uint64_t*>(h.done_ring);
+      st_release_sys_u64(&dr[h.seq % kDoneRing], h.seq + 1);
+    }
+  }
+  // complete only after the previous grid in the stream has (stream order)
+  gdc_wait();
+}
+
+}  // namespace gpuos

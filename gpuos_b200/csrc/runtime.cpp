@@ -25,6 +25,9 @@ extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::B
 extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, cudaStream_t stream);
 extern "C" cudaError_t gpuos_occupancy(int* batch_blocks_per_sm, int* worker_blocks_per_sm);
 extern "C" int gpuos_cta_threads();
+extern "C" cudaError_t gpuos_launch_lean(const void* params, int size_class, int grid,
+                                         cudaStream_t stream);
+extern "C" size_t gpuos_lean_params_size(int size_class);
 
 namespace gpuos {
 
@@ -352,7 +355,9 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   sync_timeout_s_ = opt_.sync_timeout_s > 0 ? opt_.sync_timeout_s
                                             : env_double("GPUOS_SYNC_TIMEOUT_S", 60.0);
   // every wait inside a kernel gives up after this long and reports an error
-  wait_limit_ns_ = (uint64_t)(std::min(std::max(sync_timeout_s_, 1.0), 10.0) * 1e9);
+  wait_limit_ns_ = opt_.wait_limit_us > 0
+                       ? (uint64_t)opt_.wait_limit_us * 1000ull
+                       : (uint64_t)(std::min(std::max(sync_timeout_s_, 1.0), 10.0) * 1e9);
 
   GCU(cudaFree(nullptr));
   GCU(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, device));
@@ -367,6 +372,9 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   grid_ = sm_count_ * wbps;
   const int ctas = opt_.mode == GPUOS_MODE_PERSISTENT ? grid_ - 1 : sm_count_ * batch_bps_;
   total_warps_ = ctas * gpuos_cta_threads() / 32;
+  lean_grid_ = sm_count_;
+  lean_on_ = env_double("GPUOS_LEAN", 1.0) != 0.0;
+  lean_buf_.resize(gpuos_lean_params_size(2));
 
   GCU(cudaStreamCreateWithFlags(&s_worker_, cudaStreamNonBlocking));
   GCU(cudaStreamCreateWithFlags(&s_ctrl_, cudaStreamNonBlocking));
@@ -771,9 +779,22 @@ void Executor::reclaim() {
     // a batch is done once the event recorded after its launch has completed;
     // the kernel posts a completion word only for a batch with errors
     while (done_wm_ < next_seq_) {
+      uint32_t e = 0;
+      if (lean_seq_[done_wm_ % kDoneRing]) {
+        // a lean batch posts seq + 1 when its last CTA is done
+        const uint64_t w = done_ring_[done_wm_ % kDoneRing];
+        if ((w & kDoneMask) != done_wm_ + 1) break;
+        e = (uint32_t)((w >> 48) & 0xffu);
+        if (e) {
+          ++errors_;
+          if (err_seq_ == UINT64_MAX) err_seq_ = done_wm_;
+          err_bits_ |= e;
+        }
+        ++done_wm_;
+        continue;
+      }
       const cudaError_t q = cudaEventQuery(done_ev_[done_wm_ % kDoneRing]);
       if (q == cudaErrorNotReady) break;
-      uint32_t e = 0;
       if (q != cudaSuccess) {
         e = ERR_CUDA;
         if (cuda_err_.empty()) cuda_err_ = cudaGetErrorString(q);
@@ -958,7 +979,16 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       ew_work += (uint64_t)p.r.numel << cost_log2[r];
     }
   }
-  const uint64_t warps = (uint64_t)std::max(1, total_warps_);
+  // a lean batch: the whole batch in the lean kernel's parameters (lean.cuh)
+  bool lean = lean_on_ && opt_.mode == GPUOS_MODE_STREAM && !staged && n <= (uint32_t)kLeanMaxReq;
+  for (uint32_t r = 0; r < n && lean; ++r) lean = lean_eligible(reqs[i + r], var[r]);
+  if (lean) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    GCU(cudaStreamIsCapturing(stream, &cap));
+    lean = cap == cudaStreamCaptureStatusNone;
+  }
+  const uint64_t warps = lean ? (uint64_t)lean_grid_ * (kLeanThreads / 32)
+                              : (uint64_t)std::max(1, total_warps_);
   uint64_t ce = align_up(std::max<uint64_t>(1, ew_work / (2 * warps)), 512);
   ce = std::min<uint64_t>(std::max<uint64_t>(ce, 512), 8192);
   // A batch with stage barriers runs its stages one after another, each on
@@ -1006,6 +1036,17 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       for (uint32_t r = s0; r < s1; ++r) order[s0 + counts[key(r)]++] = r;
       s0 = s1;
     }
+  }
+  if (lean) {
+    uint64_t lchunks = 0;
+    for (uint32_t r = 0; r < n; ++r) lchunks += reqs[i + r].nchunk;
+    if (publish_lean(lk, reqs, i, n, var, order, lchunks, stream)) return;
+  }
+  if (opt_.mode == GPUOS_MODE_STREAM) {
+    // a batch that is not lean runs after everything before it on the stream
+    lean_prev_in_flush_ = false;
+    lean_out_.clear();
+    lean_in_.clear();
   }
   // payload layout
   std::vector<uint32_t> cb(n + 1);
@@ -1110,6 +1151,14 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   if (staged) {
     uint32_t* w = reinterpret_cast<uint32_t*>(base + wait_off);
     for (uint32_t r = 0; r < n; ++r) w[r] = stage_first[r] ? cb[stage_first[r]] : 0u;
+    if (stall_next_) {
+      // fault injection: the last stage waits for one chunk more than the
+      // earlier stages have, which only its own (waiting) chunks could add
+      stall_next_ = false;
+      const uint32_t last = stage_first[n - 1];
+      for (uint32_t r = 0; r < n; ++r)
+        if (stage_first[order[r]] == last) w[r] = cb[last] + 1u;
+    }
   }
   const bool jit_batch = var[0] >= V_JIT_BASE;  // a batch is all custom or all precompiled
   if (jit_batch && opt_.mode == GPUOS_MODE_PERSISTENT) {
@@ -1186,12 +1235,173 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       timed_.emplace_back(e0, e1);
     }
     // completion (and the reuse of the batch's staging memory) is this event
+    lean_seq_[seq % kDoneRing] = 0;
     cudaEvent_t& de = done_ev_[seq % kDoneRing];
     if (!de) GCU(cudaEventCreateWithFlags(&de, cudaEventDisableTiming));
     GCU(cudaEventRecord(de, stream));
     last_stream_ = stream;
     have_last_stream_ = true;
   }
+}
+
+namespace {
+bool variant_binary(int v) {
+  return v == V_ADD || v == V_MUL || v == V_SUB || v == V_DIV0 || v == V_DIV || v == V_MAX ||
+         v == V_MIN || v == V_POW;
+}
+
+// (p0, p1) a request runs with: its own, or its slot's when it names a slot
+void effective_params(const Tables& tab, const Req& q, float* p0, float* p1) {
+  *p0 = q.p0;
+  *p1 = q.p1;
+  if (q.flags & RF_SLOT) {
+    const int s = q.op;
+    const int phys = (s >= 0 && s < kMaxSlots) ? tab.alias[s] : -1;
+    if (phys >= 0 && phys < kMaxSlots) {
+      *p0 = tab.slot[phys].p0;
+      *p1 = tab.slot[phys].p1;
+    }
+  }
+}
+
+template <int N>
+void fill_lean(uint8_t* buf, uint64_t seq, uint64_t st, uint64_t done_ring, uint32_t flags,
+               const std::vector<Pending>& reqs, size_t i, uint32_t n, const std::vector<int>& var,
+               const std::vector<uint32_t>& order, uint64_t nchunk, const Tables& tab) {
+  LeanBatch<N>* b = reinterpret_cast<LeanBatch<N>*>(buf);
+  std::memset(&b->h, 0, sizeof(b->h));
+  b->h.seq = seq;
+  b->h.st = st;
+  b->h.done_ring = done_ring;
+  b->h.nreq = n;
+  b->h.nchunk = (uint32_t)nchunk;
+  b->h.flags = flags;
+  int npar = 0;
+  uint32_t c = 0;
+  for (uint32_t r = 0; r < n; ++r) {
+    const Pending& p = reqs[i + order[r]];
+    float p0, p1;
+    effective_params(tab, p.r, &p0, &p1);
+    int k = 0;
+    while (k < npar && !(b->h.par[k][0] == p0 && b->h.par[k][1] == p1)) ++k;
+    if (k == npar) {
+      b->h.par[k][0] = p0;
+      b->h.par[k][1] = p1;
+      ++npar;
+    }
+    LeanRec& q = b->rec[r];
+    q.a = p.r.a;
+    q.b = p.r.b;
+    q.o = p.r.o;
+    q.numel = (uint32_t)p.r.numel;
+    q.chunk = p.r.chunk;
+    q.op = (uint8_t)var[order[r]];
+    q.flags = (uint8_t)(p.r.flags & RF_HAS_B);
+    q.pidx = (uint8_t)k;
+    b->cb[r] = c;
+    c += p.nchunk;
+  }
+  b->cb[n] = c;
+}
+}  // namespace
+
+// A request the lean kernel can run: contiguous, 16-byte aligned fp32 tensors
+// (no scalar operands) of a precompiled elementwise operator, with B present
+// when the operator reads it.
+bool Executor::lean_eligible(const Pending& p, int v) const {
+  const Req& q = p.r;
+  if (q.kind != RK_EW || q.layout != EL_CONTIG || !(q.flags & RF_VEC) || p.has_ext) return false;
+  if (q.flags & (RF_A_SCALAR | RF_B_SCALAR)) return false;
+  if (v < 0 || v >= V_NUM_EW || q.numel >= (1ll << 31)) return false;
+  if (q.dta != kF32 || q.dto != kF32) return false;
+  const bool hasb = q.flags & RF_HAS_B;
+  if (hasb && q.dtb != kF32) return false;
+  if (variant_binary(v) && !hasb) return false;
+  return true;
+}
+
+// Publish one lean batch.  Returns false (nothing published) when its
+// parameters do not fit the block (more than kLeanPar distinct pairs).
+bool Executor::publish_lean(std::unique_lock<std::mutex>& lk, std::vector<Pending>& reqs,
+                            size_t i, uint32_t n, const std::vector<int>& var,
+                            const std::vector<uint32_t>& order, uint64_t nchunk,
+                            cudaStream_t stream) {
+  {
+    std::vector<std::pair<float, float>> pars;
+    for (uint32_t r = 0; r < n; ++r) {
+      float p0, p1;
+      effective_params(tab_, reqs[i + r].r, &p0, &p1);
+      if (std::find(pars.begin(), pars.end(), std::make_pair(p0, p1)) == pars.end())
+        pars.emplace_back(p0, p1);
+      if (pars.size() > (size_t)kLeanPar) return false;
+    }
+  }
+  if (nchunk == 0 || nchunk > 0x7fffffffull) return false;
+  // a free batch slot (counters and completion word)
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int it = 0;; ++it) {
+    reclaim();
+    if (next_seq_ - retired_wm_ < (uint64_t)kDoneRing - 1) break;
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() >
+        sync_timeout_s_)
+      throw GError(GPUOS_ETIMEOUT, "timed out waiting for a free batch slot");
+    lk.unlock();
+    if (it < 64) GPUOS_PAUSE();
+    else std::this_thread::sleep_for(std::chrono::microseconds(20));
+    lk.lock();
+  }
+  const uint64_t seq = next_seq_;
+  // wait for the previous grid unless it is a lean batch of this flush that
+  // shares no memory with this one
+  bool wf = !lean_prev_in_flush_;
+  for (uint32_t r = 0; r < n && !wf; ++r) {
+    const Pending& p = reqs[i + r];
+    wf = lean_out_.overlaps(p.out_ext) || lean_in_.overlaps(p.out_ext);
+    for (int k = 0; k < p.nin && !wf; ++k) wf = lean_out_.overlaps(p.in_ext[k]);
+  }
+  const int cls = n <= 32 ? 0 : (n <= 128 ? 1 : 2);
+  const uint64_t st = reinterpret_cast<uint64_t>(states_ + seq % kDoneRing);
+  const uint64_t dr = reinterpret_cast<uint64_t>(
+      hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));
+  const uint32_t flags = wf ? LEAN_WAIT_FIRST : 0u;
+  uint8_t* buf = lean_buf_.data();
+  if (cls == 0) fill_lean<32>(buf, seq, st, dr, flags, reqs, i, n, var, order, nchunk, tab_);
+  else if (cls == 1) fill_lean<128>(buf, seq, st, dr, flags, reqs, i, n, var, order, nchunk, tab_);
+  else fill_lean<kLeanMaxReq>(buf, seq, st, dr, flags, reqs, i, n, var, order, nchunk, tab_);
+  DeviceGuard g(device_);
+  if (have_last_stream_ && stream != last_stream_ && done_wm_ < seq) {
+    GCU(cudaEventRecord(last_event_, last_stream_));
+    GCU(cudaStreamWaitEvent(stream, last_event_, 0));
+  }
+  const int grid = (int)std::min<uint64_t>((uint64_t)lean_grid_, std::max<uint64_t>(1, nchunk / 32));
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (timing_) {
+    for (cudaEvent_t* e : {&e0, &e1}) {
+      if (ev_pool_.empty()) {
+        GCU(cudaEventCreate(e));
+      } else {
+        *e = ev_pool_.back();
+        ev_pool_.pop_back();
+      }
+    }
+    GCU(cudaEventRecord(e0, stream));
+  }
+  lean_seq_[seq % kDoneRing] = 1;
+  GCU(gpuos_launch_lean(buf, cls, grid, stream));
+  if (timing_) {
+    GCU(cudaEventRecord(e1, stream));
+    timed_.emplace_back(e0, e1);
+  }
+  next_seq_ = seq + 1;
+  ++lean_count_;
+  lean_prev_in_flush_ = !timing_;
+  for (uint32_t r = 0; r < n; ++r) {
+    lean_out_.add(reqs[i + r].out_ext);
+    for (int k = 0; k < reqs[i + r].nin; ++k) lean_in_.add(reqs[i + r].in_ext[k]);
+  }
+  last_stream_ = stream;
+  have_last_stream_ = true;
+  return true;
 }
 
 // The variant a request's record will carry (its slot resolved now).
@@ -1285,11 +1495,18 @@ uint64_t Executor::flush(bool sync, cudaStream_t stream) {
       }
       size_t i = 0;
       const uint64_t budget = arena_bytes_ / 4;
+      lean_prev_in_flush_ = false;
+      lean_out_.clear();
+      lean_in_.clear();
+      // stream mode: batches no larger than a lean parameter block holds
+      const size_t cap = (opt_.mode == GPUOS_MODE_STREAM && lean_on_)
+                             ? std::min<size_t>(opt_.max_batch, kLeanMaxReq)
+                             : (size_t)opt_.max_batch;
       while (i < reqs.size()) {
         size_t j = i;
         uint64_t bytes = 256, floats = 0, cnts = 0, chunks = 0;
         const bool jit = variant_of(reqs[i]) >= V_JIT_BASE;
-        while (j < reqs.size() && j - i < (size_t)opt_.max_batch) {
+        while (j < reqs.size() && j - i < cap) {
           const Pending& p = reqs[j];
           if (j > i && (variant_of(p) >= V_JIT_BASE) != jit) break;
           const uint64_t b = 136 + (p.has_ext ? sizeof(ExtRec) : 0);
@@ -1338,6 +1555,15 @@ void Executor::wait(uint64_t ticket, double timeout_s) {
         return;
       }
       if (opt_.mode == GPUOS_MODE_PERSISTENT) ensure_worker_locked();
+      if (opt_.mode == GPUOS_MODE_STREAM && (it & 1023) == 1023 && have_last_stream_) {
+        // a lean batch completes through its word only: a kernel that failed
+        // never writes it, so look at the stream's error state now and then
+        DeviceGuard g(device_);
+        const cudaError_t q = cudaStreamQuery(last_stream_);
+        if (q != cudaSuccess && q != cudaErrorNotReady)
+          throw GError(GPUOS_ECUDA, std::string("the batch stream reported: ") +
+                                        cudaGetErrorString(q));
+      }
     }
     const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     if (el > timeout_s)
@@ -1519,6 +1745,11 @@ void Executor::set_debug_level(int level) {
   hctrl_->debug_level = (uint32_t)level;
 }
 
+void Executor::stall_next_batch() {
+  std::lock_guard<std::mutex> lk(mu_);
+  stall_next_ = true;
+}
+
 void Executor::stats(gpuos_stats* out) {
   std::lock_guard<std::mutex> lk(mu_);
   reclaim();
@@ -1533,6 +1764,7 @@ void Executor::stats(gpuos_stats* out) {
   out->errors = errors_;
   out->relaunches = relaunches_;
   out->dev_ns = dev_ns_;
+  out->lean = lean_count_;
   out->capacity = opt_.capacity;
   out->max_batch = opt_.max_batch;
   out->mode = opt_.mode;
@@ -1783,6 +2015,10 @@ int32_t gpuos_set_yield_every(gpuos_executor* ex, uint64_t every) {
 
 int32_t gpuos_set_debug_level(gpuos_executor* ex, int32_t level) {
   return guard([&] { X(ex)->set_debug_level(level); });
+}
+
+int32_t gpuos_debug_stall_next_batch(gpuos_executor* ex) {
+  return guard([&] { X(ex)->stall_next_batch(); });
 }
 
 int32_t gpuos_worker_alive(gpuos_executor* ex) {

@@ -132,6 +132,7 @@ class Executor {
   // worker control
   void set_yield_every(uint64_t every);
   void set_debug_level(int level);
+  void stall_next_batch();
   bool worker_alive();
   void stats(gpuos_stats* out);
   void shutdown();
@@ -141,6 +142,10 @@ class Executor {
  private:
   void publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& reqs, size_t i, size_t j,
                cudaStream_t stream);
+  bool lean_eligible(const Pending& p, int v) const;
+  bool publish_lean(std::unique_lock<std::mutex>& lk, std::vector<Pending>& reqs, size_t i,
+                    uint32_t n, const std::vector<int>& var, const std::vector<uint32_t>& order,
+                    uint64_t nchunk, cudaStream_t stream);
   uint32_t take_batch_err(uint64_t seq);
   void reclaim();
   void ensure_worker_locked();
@@ -222,7 +227,18 @@ class Executor {
   uint64_t requests_ = 0;
   uint64_t errors_ = 0;
   uint64_t dev_ns_ = 0;
+  uint64_t lean_count_ = 0;
   int debug_level_ = 0;
+  bool stall_next_ = false;  // fault injection: next staged batch waits for a chunk that never comes
+
+  // lean batches (stream mode): whole batch in the kernel's parameters, launched
+  // with programmatic dependent launch, completed by a word in done_ring_
+  bool lean_on_ = true;
+  int lean_grid_ = 0;                 // CTAs of the lean kernel (one per SM)
+  std::vector<uint8_t> lean_seq_ = std::vector<uint8_t>(kDoneRing, 0);  // batch seq is lean
+  std::vector<uint8_t> lean_buf_;     // parameter block being built (largest size class)
+  bool lean_prev_in_flush_ = false;   // the last op this flush put on the stream is a lean batch
+  IntervalSet lean_out_, lean_in_;    // extents of this flush's lean batches
 };
 
 // Request planning (no GPU needed): broadcasting, dim coalescing, layout

@@ -68,7 +68,11 @@ typedef struct gpuos_options {
   double idle_ms;            /* persistent worker exits after this long idle (0 = default) */
   double sync_timeout_s;     /* bound on every host wait (0 = default) */
   int32_t max_batch;         /* requests per batch (reference GPUOS_BATCH_SHARD, default 512) */
-  int32_t reserved[7];
+  int32_t wait_limit_us;     /* bound of every wait inside a kernel, in microseconds (a stage
+                                barrier, an earlier batch); on expiry the batch completes with
+                                an error.  0 = default: sync_timeout_s clamped to [1, 10] s.
+                                (The reference's waits are unbounded.) */
+  int32_t reserved[6];
 } gpuos_options;
 
 typedef struct gpuos_stats {
@@ -82,6 +86,7 @@ typedef struct gpuos_stats {
   uint64_t errors;      /* device-reported request errors */
   uint64_t relaunches;  /* persistent worker launches */
   uint64_t dev_ns;      /* device time of completed batches (first claim -> last chunk) */
+  uint64_t lean;        /* stream-mode batches run by the lean kernel (parameters only) */
   int32_t capacity;
   int32_t max_batch;
   int32_t mode;
@@ -180,6 +185,14 @@ int32_t gpuos_variant_by_name(const char* name);
  * *n_out.  (No counterpart in the reference, which has no kernel timing.) */
 int32_t gpuos_set_timing(gpuos_executor* ex, int32_t on);
 int32_t gpuos_take_timings(gpuos_executor* ex, float* ms, uint64_t cap, uint64_t* n_out);
+
+/* Fault injection for tests of the bounded waits (no counterpart in the
+ * reference, whose waits are unbounded): the next batch published with stage
+ * barriers gets one stage wait that no chunk can meet.  The kernel's bounded
+ * wait runs out after wait_limit_us, the batch records a stage-timeout error
+ * and completes, and the next synchronous flush or wait returns
+ * GPUOS_EDEVICE.  The executor stays usable. */
+int32_t gpuos_debug_stall_next_batch(gpuos_executor* ex);
 
 /* Worker control (replaces gpu_set_yield_every_async / gpu_set_debug_level_async,
  * persistent_kernel.cu:232-238, and worker_alive(), gpuos_ext.cpp:128-135). */
