@@ -11,18 +11,27 @@ request) and flushed every 512 requests, ending with flush(sync=True).
 Printed (rank 0, one JSON line):
   value      requests/s of the whole job with inputs resident in HBM, timed
              with CUDA events on the submitting stream, max over ranks
+  check      the last timed step's whole output slab against the oracle
+             (bit-exact operators bit for bit); a mismatch exits non-zero
   e2e        the same with host buffers: pinned host -> device copy of every
              input and device -> host copy of every output inside each step
-  roofline   the batch kernel (stream mode) timed per launch with CUDA events
-             around each launch: algorithmic bytes / launch time vs the
-             measured HBM copy bandwidth
+  roofline   the batch kernel in stream mode: each step's batches are
+             published while a spin kernel holds the stream, so that they run
+             back to back, and one event pair brackets them; the average
+             launch duration is that region over the launches in it
+             (algorithmic bytes / launch time vs the measured HBM copy
+             bandwidth); by_workload does the same for the other
+             configurations' streams
+  persistent the same stream through the persistent worker
   cpu_baseline   the CPU oracle (a C port of the reference algorithm) on all
-             host cores, same stream
+             host cores, and PyTorch eager on the same cores, same stream
   flush_p50_us   latency of a one-request flush(sync=True) and of a 1024 x 4096
              add/mul flush, median of repeats
+  decode_chain   the transformer-decode pointwise chain (bf16, 32 layers)
 With --impl reference the same stream runs on the CPU restatement of the
-reference's algorithm (the reference has no CPU path of its own; its GPU path
-is not a library this harness can drive safely).
+reference's algorithm: the reference has no CPU path of its own, and its GPU
+path needs its persistent worker, whose harness synchronises the whole device
+while that kernel runs.
 """
 from __future__ import annotations
 
@@ -323,6 +332,118 @@ def run_step(ext, calls, flush_every):
     ext.flush(sync=True)
 
 
+EXACT_OPS = {"add", "mul", "sub", "div0", "div", "maximum", "minimum", "relu", "abs",
+             "hardsigmoid", "hardswish", "leaky_relu", "clamp", "clamp_min", "clamp_max", "copy",
+             "sqrt"}
+
+
+def check_outputs(stream, host_out):
+    """The checker: the whole output slab of the last timed step against the
+    oracle (the C restatement of the reference algorithm, run over the same
+    stream on the host).  Exact operators must match bit for bit; the
+    transcendental ones within 4e-6 * (|ref| + |A| + |B| + 1): CUDA's math
+    functions and the host's differ in the last bits, and a formula such as
+    elu's expf(A) - 1 cancels them into a larger relative difference near 0.
+    The strict per-operator bounds are checked by the tests."""
+    import oracle
+    ref = torch.zeros(stream.out_bytes, dtype=torch.uint8)
+    items = [(0 if r.kind == "ew" else 1, r.op, r.p0, r.p1, r.a.view(stream.host_in),
+              r.b.view(stream.host_in) if r.b is not None else None, r.out.view(ref),
+              list(r.axes), r.keepdim) for r in stream.requests]
+    oracle.run(oracle.make_reqs(items), 0)
+    exact = approx = 0
+    bad = []
+    worst = 0.0
+    for i, r in enumerate(stream.requests):
+        g, w = r.out.view(host_out), r.out.view(ref)
+        if r.kind != "ew":
+            continue
+        if r.op in EXACT_OPS:
+            iv = torch.int32 if g.dtype == torch.float32 else torch.int16
+            if not torch.equal(g.contiguous().view(iv), w.contiguous().view(iv)):
+                bad.append(i)
+            exact += 1
+            continue
+        a = r.a.view(stream.host_in).float()
+        scale = w.double().abs() + torch.broadcast_to(a, g.shape).double().abs()
+        if r.b is not None:
+            scale = scale + torch.broadcast_to(r.b.view(stream.host_in).float(), g.shape).double().abs()
+        err = (g.double() - w.double()).abs()
+        nan_ok = torch.isnan(g) == torch.isnan(w)
+        err = torch.where(torch.isnan(g) & torch.isnan(w), torch.zeros_like(err), err)
+        # the absolute floor covers cancellation (elu's expf(A) - 1 near 0)
+        ratio = float((err / (4e-6 * (scale + 1.0))).max()) if err.numel() else 0.0
+        worst = max(worst, ratio)
+        if ratio > 1.0 or not bool(nan_ok.all()):
+            bad.append(i)
+        approx += 1
+    return {"requests": len(stream.requests), "bit_exact": exact, "within_tolerance": approx,
+            "worst_ratio": round(worst, 4), "mismatched": len(bad), "first_mismatches": bad[:5],
+            "ok": not bad}
+
+
+def _torch_eager_calls(stream, out):
+    """The stream as PyTorch eager CPU calls on the host tensors (the
+    baseline the reference compares against): one torch op per request,
+    written into the request's output view."""
+    import torch.nn.functional as F
+    un = {"sigmoid": torch.sigmoid, "tanh": torch.tanh, "exp": torch.exp, "log": torch.log,
+          "sqrt": torch.sqrt, "abs": torch.abs, "sin": torch.sin, "cos": torch.cos}
+    bi = {"add": torch.add, "sub": torch.sub, "mul": torch.mul, "div0": torch.div,
+          "div": torch.div, "maximum": torch.maximum, "minimum": torch.minimum, "pow": torch.pow}
+    calls = []
+    for r in stream.requests:
+        a = r.a.view(stream.host_in)
+        o = r.out.view(out)
+        if r.kind == "reduce":
+            fn = torch.sum if r.op == "sum" else torch.mean
+            calls.append(lambda a=a, o=o, fn=fn, ax=list(r.axes), k=r.keepdim:
+                         fn(a, dim=ax, keepdim=k, out=o))
+        elif r.op in bi:
+            b = r.b.view(stream.host_in)
+            calls.append(lambda a=a, b=b, o=o, fn=bi[r.op]: fn(a, b, out=o))
+        elif r.op in un:
+            calls.append(lambda a=a, o=o, fn=un[r.op]: fn(a, out=o))
+        elif r.op == "relu":
+            calls.append(lambda a=a, o=o: torch.clamp_min(a, 0.0, out=o))
+        elif r.op == "clamp":
+            calls.append(lambda a=a, o=o, lo=r.p0, hi=r.p1: torch.clamp(a, lo, hi, out=o))
+        else:
+            f = {"gelu": lambda x: F.gelu(x, approximate="tanh"), "hardsigmoid": F.hardsigmoid,
+                 "hardswish": F.hardswish, "leaky_relu": lambda x, p=r.p0: F.leaky_relu(x, p),
+                 "elu": lambda x, p=r.p0: F.elu(x, p), "softplus": lambda x, p=r.p0: F.softplus(x, p)}[r.op]
+            calls.append(lambda a=a, o=o, f=f: o.copy_(f(a)))
+    return calls
+
+
+def torch_eager_baseline(stream, min_seconds=5.0):
+    """PyTorch eager on the host's cores, the same stream, whole passes until
+    min_seconds of wall time (at least one)."""
+    cores = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(cores)
+    try:
+        out = torch.empty(stream.out_bytes, dtype=torch.uint8)
+        calls = _torch_eager_calls(stream, out)
+        for c in calls[:256]:
+            c()
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            for c in calls:
+                c()
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= min_seconds:
+                break
+    finally:
+        torch.set_num_threads(prev)
+    return {"value": round(reps * len(stream.requests) / el, 1), "unit": "requests/s",
+            "cores": cores, "kind": "torch_eager_cpu",
+            "sample": f"{reps} full passes of the {len(stream.requests)}-request stream "
+                      f"({el:.1f} s wall, torch {torch.__version__}, "
+                      f"torch.set_num_threads({cores}))"}
+
+
 def cpu_baseline(stream, min_seconds=5.0):
     """The CPU port of the reference algorithm on every host core."""
     import oracle
@@ -567,12 +688,12 @@ def bench_ours(args, world, rank, local):
     wall = time.perf_counter() - t0
     q1 = ext.peek_queue()
     ev_s = ev0.elapsed_time(ev1) / 1e3
+    host_out = dout.cpu()  # the last timed step's outputs, checked below
     t_step = allmax(max(ev_s, wall) / args.steps, world)  # per step, slowest rank
     torch.cuda.synchronize()
     clk = clocks.stop()
     batches = q1["tail"] - q0["tail"]
     launches = batches if args.mode == "stream" else max(1, q1["relaunches"] - q0["relaunches"])
-    # outputs of the last step are checked against the oracle on a sample
     value = world * n_req / t_step
 
     # e2e: host buffers, H2D of the inputs and D2H of the outputs every step,
@@ -600,18 +721,40 @@ def bench_ours(args, world, rank, local):
     ext.shutdown()
 
     peak, peak_kind = peaks()
-    roof = roofline_leg(stream, dev, max(2, min(args.steps, 5)), peak, peak_kind)
-    traffic = ROOT / "profiles" / "traffic.json"
-    if traffic.exists():
+    rsteps = max(2, min(args.steps, 5))
+    roof = roofline_leg(stream, dev, rsteps, peak, peak_kind)
+    traffic = {}
+    tpath = ROOT / "profiles" / "traffic.json"
+    if tpath.exists():
         try:
-            tr = json.loads(traffic.read_text())
-            roof["traffic"] = tr.get(args.workload)
+            traffic = json.loads(tpath.read_text())
         except (ValueError, OSError):
-            pass
+            traffic = {}
+    roof["traffic"] = traffic.get(args.workload)
+    # the other configurations' batch kernels, the same way (the two large
+    # streams with inputs drawn on the device)
+    if rank == 0 and not args.no_by_workload:
+        from gpuos_b200 import workloads as W
+        byw = {args.workload: {k: roof[k] for k in ("frac", "achieved", "avg_launch_us",
+                                                    "bytes_per_launch", "launches", "kernel")}}
+        for name in ("micro_add_mul", "broadcast_mixed", "lastdim_reduce"):
+            if name == args.workload:
+                continue
+            st = W.STREAMS[name]() if name == "micro_add_mul" else W.STREAMS[name](fill=False)
+            r = roofline_leg(st, dev, rsteps, peak, peak_kind)
+            byw[name] = {k: r[k] for k in ("frac", "achieved", "avg_launch_us", "bytes_per_launch",
+                                           "launches", "kernel")}
+            byw[name]["traffic"] = traffic.get(name)
+            del st
+            torch.cuda.empty_cache()
+        roof["by_workload"] = byw
 
     if rank != 0:
         return None
+    check = check_outputs(stream, host_out)
     cpu = cpu_baseline(stream) if world == 1 else None
+    if cpu is not None:
+        cpu["torch_eager"] = torch_eager_baseline(stream)
     return {
         "metric": "micro-ops/sec (requests/s) of the 16K mixed-op request stream",
         "value": round(value, 1),
@@ -623,7 +766,7 @@ def bench_ours(args, world, rank, local):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": stream.meta.get("dtype", "f32"),
         "data": "synthetic (seed 0)",
         "config": {"workload": workload_desc(args.workload, stream),
                    "mode": args.mode, "api": "gpuos_ext.submit_* per request",
@@ -636,6 +779,7 @@ def bench_ours(args, world, rank, local):
         "cpu_baseline": cpu,
         "flush_p50_us": lat,
         "decode_chain": chain,
+        "check": check,
         "gpu_launches": int(launches * world),
         "clocks": clk,
     }
@@ -666,7 +810,8 @@ def bench_reference(args, world, rank):
         "metric": "micro-ops/sec (requests/s) of the 16K mixed-op request stream",
         "value": round(v, 1), "unit": "requests/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": stream.meta.get("dtype", "f32"),
         "data": "synthetic (seed 0)",
         "config": {"workload": workload_desc(args.workload, stream),
                    "engine": "liboracle.so (C port of the reference algorithm), all host cores"},
@@ -678,32 +823,38 @@ def bench_reference(args, world, rank):
 
 
 def profile_case(dev="cuda:0"):
-    """The small case the committed ncu captures use: two stream-mode launches
-    of gpuos_batch_kernel on one executor.  Launch 0: 2048 fp32 adds of 8192
-    elements in one batch (201 MB).  Launch 1: the first batch of the bench's
-    mixed 24-operator stream (its first 512 requests, seed 0), exactly as
-    the bench runs it.  A 256 MB write before each launch evicts its inputs
-    from L2.  About 1.5 GB on the device."""
+    """The small case the committed ncu captures use, in stream mode, with a
+    256 MB write before each step that evicts its inputs from L2:
+      launches 0-1  the whole add/mul stream (1024 x 4096 fp32; two lean
+                    batches of 512 requests, 25 MB each)
+      launch 2      the first batch of the mixed 24-operator stream (its first
+                    512 requests, seed 0), exactly as the bench runs it
+      launch 3      the first 512 requests of the broadcast stream
+      launch 4      the first 512 requests of the reduction stream
+    About 4 GB on the device."""
     import gpuos_b200.cabi as C
     from gpuos_b200 import workloads as W
     scrub = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 2 x L2: evicts the inputs
-    st = W.mixed_24op(seed=0)
-    fe = st.flush_every
-    with C.Executor(0, mode=C.MODE_STREAM, max_batch=2048) as e:
-        A = torch.randn(2048, 8192, device=dev)
-        B = torch.randn(2048, 8192, device=dev)
-        O = torch.empty(2048, 8192, device=dev)
-        din, dout = st.device_buffers(dev)
-        calls = W.Submitter(_CabiExt(e)).prepare(st, st.views(din, dout))[:fe]
-        scrub.fill_(1)
-        for i in range(2048):
-            e.builtin(C.OP_ADD, A[i], B[i], O[i])
-        e.flush(sync=True)
-        scrub.fill_(2)
-        for fn, a in calls:
-            fn(*a)
-        e.flush(sync=True)
-        assert torch.equal(O, A + B)
+    with C.Executor(0, mode=C.MODE_STREAM) as e:
+        sub = W.Submitter(_CabiExt(e))
+        for k, (name, kw) in enumerate((("micro_add_mul", {}), ("mixed_24op", {}),
+                                        ("broadcast_mixed", {"fill": False}),
+                                        ("lastdim_reduce", {"fill": False}))):
+            st = W.STREAMS[name](**kw)
+            if name != "micro_add_mul":
+                st = st.head(st.flush_every)
+            din, dout = st.device_buffers(dev)
+            calls = sub.prepare(st, st.views(din, dout))
+            scrub.fill_(k)
+            for fn, a in calls:
+                fn(*a)
+            e.flush(sync=True)
+            if name == "micro_add_mul":
+                out = dout.cpu()
+                for r in st.requests[:8]:
+                    x, y = r.a.view(st.host_in), r.b.view(st.host_in)
+                    assert torch.equal(r.out.view(out), x + y if r.op == "add" else x * y)
+            del din, dout
     print("profile case done", flush=True)
 
 
@@ -716,6 +867,8 @@ def main():
     ap.add_argument("--mode", default=os.environ.get("GPUOS_MODE", "stream"),
                     choices=["persistent", "stream"])
     ap.add_argument("--workload", default="mixed_24op")
+    ap.add_argument("--no-by-workload", action="store_true",
+                    help="time only the headline stream's batch kernel in the roofline leg")
     ap.add_argument("--profile-case", action="store_true",
                     help="run the small two-launch case of the committed ncu captures and exit")
     args = ap.parse_args()
@@ -737,6 +890,8 @@ def main():
             dist.destroy_process_group()
     if res is not None:
         print(json.dumps(res), flush=True)
+        if res.get("check") is not None and not res["check"]["ok"]:
+            sys.exit("bench: the outputs of the timed steps differ from the oracle's")
 
 
 if __name__ == "__main__":

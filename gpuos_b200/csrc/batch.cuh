@@ -76,9 +76,15 @@ __device__ __forceinline__ void decode(Cur& cur, const Exec& ex, const Req* rec,
   }
 }
 
-__device__ __forceinline__ void run_chunk(const Exec& ex, const Cur& cur, uint32_t k,
+__device__ __forceinline__ void run_chunk(const Exec& ex, Cur& cur, uint32_t k,
                                           const ExtRec* xs) {
   if (cur.vec) {
+    if (ex.flags & BF_STAGED) {
+      // a scalar operand can be the output of an earlier stage: read it after
+      // this chunk's stage wait, not when the record was decoded
+      if (cur.u.ma == OM_SCALAR) cur.u.As = ld1(cur.u.a, cur.u.dta, 0);
+      if (cur.u.mb == OM_SCALAR && (cur.u.flags & RF_HAS_B)) cur.u.Bs = ld1(cur.u.b, cur.u.dtb, 0);
+    }
     const int64_t e0 = (int64_t)k * cur.u.chunk;
     int64_t n = cur.u.numel - e0;
     if (n > (int64_t)cur.u.chunk) n = cur.u.chunk;
@@ -222,6 +228,7 @@ __device__ __forceinline__ void cta_leave_batch(const Exec& ex, uint32_t* cta_ch
       ex.st->claim = 0;
       ex.st->done = 0;
       ex.st->err = 0;
+      ex.st->nt0 = 0;
       ex.st->ctas_left = 0;
       if (retired_ring) st_release_sys_u64(&retired_ring[ex.seq % kDoneRing], ex.seq + 1);
     }

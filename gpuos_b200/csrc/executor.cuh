@@ -1,7 +1,7 @@
 // Batch executor building blocks: request records, jump-table resolution,
-// and the per-warp chunk processors (strided elementwise, reductions).  The
-// CTA pipeline that feeds them, and the staged vector path, are in
-// pipeline.cuh.
+// and the per-warp chunk processors (vector, 2-D tile and strided
+// elementwise bodies, reductions).  The loop that hands chunks to warps is
+// in batch.cuh; the lean kernel for fp32 contiguous batches in lean.cuh.
 //
 // Replaces the reference's op_batch (src/persistent_kernel.cu:81-112), which
 // walks the sub-tasks of a 512-task shard one after another inside a single
@@ -157,6 +157,7 @@ struct Exec {
   uint32_t* counters;           // self-cleaning combine counters
   volatile uint64_t* done_ring; // completion words in mapped host memory
   uint64_t* done_dev;           // device copy of the completion words (worker only)
+  volatile uint64_t* dur_ring;  // device time of each batch (mapped host memory), or null
   uint64_t wait_limit_ns;
   uint64_t seq;                 // batch sequence number
   uint64_t wait_from;           // BF_AFTER_PREV: batches [wait_from, seq) first
@@ -249,6 +250,124 @@ __device__ __forceinline__ void ew_generic(const ReqView& q, const ExtRec* x, in
       }
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// 2-D elementwise tiles (EL_TILE2D): a chunk is a block of `chunk` columns of
+// every one of the request's rows.  Lane l owns columns c0 + l, c0 + l + 32,
+// ... and walks down the rows kTileU at a time, all loads of a round issued
+// raw before any is converted: the output and row-contiguous operands are
+// read and written 32 adjacent columns per instruction, and a transposed
+// operand (row stride 1) is read by each lane along its own contiguous run,
+// which L1 serves for the neighbouring rows.  No division per element; the
+// dtypes and the operator are template parameters for the combinations of
+// the broadcast configuration (-1: read at run time).
+// ---------------------------------------------------------------------------
+static constexpr int kTileU = 8;
+
+template <int DT>
+__device__ __forceinline__ uint32_t t2_ld(uint64_t p, int dt, int64_t off) {
+  const int d = DT >= 0 ? DT : dt;
+  if (d == kF32) return reinterpret_cast<const uint32_t*>(p)[off];
+  return reinterpret_cast<const uint16_t*>(p)[off];
+}
+
+template <int DT>
+__device__ __forceinline__ float t2_cvt(uint32_t r, int dt) {
+  return cvt1(r, DT >= 0 ? DT : dt);
+}
+
+template <int DT>
+__device__ __forceinline__ void t2_st(uint64_t p, int dt, int64_t off, float v) {
+  st1(p, DT >= 0 ? DT : dt, off, v);
+}
+
+template <int V>
+__device__ __forceinline__ float t2_op(int v, float A, float B, float p0, float p1) {
+  if constexpr (V >= 0) {
+    return op1<V>(A, B, p0, p1);
+  } else {
+    float r = 0.f;
+    ew_apply1(v, A, B, r, p0, p1);
+    return r;
+  }
+}
+
+template <int DA, int DB, int DO, int V>
+__device__ __forceinline__ void ew_tile2d(const ReqView& q, int v, float p0, float p1, uint32_t k,
+                                          int lane) {
+  const int64_t N = q.inner, R = q.nseg;
+  const int64_t cb = (int64_t)k * q.chunk;
+  const int64_t ce = min(N, cb + (int64_t)q.chunk);
+  const bool hasb = q.flags & RF_HAS_B;
+  const bool a_sc = q.flags & RF_A_SCALAR, b_sc = q.flags & RF_B_SCALAR;
+  const int64_t sar = q.sa_row, sai = q.sa_in, sbr = q.sb_row, sbi = q.sb_in, sor = q.so_row;
+  // per-row B that does not vary along the row ([B,1]): one value per row, the
+  // same for every lane; per-column B that does not vary down the rows ([N]):
+  // one value per lane and column
+  const bool b_col = hasb && !b_sc && sbr == 0;
+#pragma unroll 1
+  for (int64_t c = cb + lane; c < ce; c += 32) {
+    const int64_t ao = a_sc ? 0 : c * sai;
+    const int64_t bo = b_sc ? 0 : c * sbi;
+    const float bcol = (hasb && (b_col || b_sc)) ? t2_cvt<DB>(t2_ld<DB>(q.b, q.dtb, bo), q.dtb) : 0.f;
+#pragma unroll 1
+    for (int64_t i0 = 0; i0 < R; i0 += kTileU) {
+      uint32_t ra[kTileU], rb[kTileU];
+#pragma unroll
+      for (int u = 0; u < kTileU; ++u) {
+        ra[u] = 0u;
+        rb[u] = 0u;
+        const int64_t i = i0 + u;
+        if (i < R) {
+          ra[u] = t2_ld<DA>(q.a, q.dta, a_sc ? 0 : ao + i * sar);
+          if (hasb && !b_col && !b_sc) rb[u] = t2_ld<DB>(q.b, q.dtb, bo + i * sbr);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kTileU; ++u) {
+        const int64_t i = i0 + u;
+        if (i < R) {
+          const float A = t2_cvt<DA>(ra[u], q.dta);
+          const float B = hasb ? ((b_col || b_sc) ? bcol : t2_cvt<DB>(rb[u], q.dtb)) : 0.f;
+          t2_st<DO>(q.o, q.dto, i * sor + c, t2_op<V>(v, A, B, p0, p1));
+        }
+      }
+    }
+  }
+}
+
+#ifndef GPUOS_JIT_LINK
+// The dtype triples of the broadcast configuration (fp32+fp32, fp16+fp32,
+// bf16+bf16, fp16+fp16) with its six operators get their own bodies; any
+// other request runs the body with run-time dtypes and operator.
+template <int DA, int DB, int DO>
+__device__ __forceinline__ void tile2d_ops(const ReqView& q, int v, float p0, float p1, uint32_t k,
+                                           int lane) {
+  switch (v) {
+    case V_ADD: ew_tile2d<DA, DB, DO, V_ADD>(q, v, p0, p1, k, lane); return;
+    case V_SUB: ew_tile2d<DA, DB, DO, V_SUB>(q, v, p0, p1, k, lane); return;
+    case V_MUL: ew_tile2d<DA, DB, DO, V_MUL>(q, v, p0, p1, k, lane); return;
+    case V_DIV0: ew_tile2d<DA, DB, DO, V_DIV0>(q, v, p0, p1, k, lane); return;
+    case V_MAX: ew_tile2d<DA, DB, DO, V_MAX>(q, v, p0, p1, k, lane); return;
+    case V_MIN: ew_tile2d<DA, DB, DO, V_MIN>(q, v, p0, p1, k, lane); return;
+    default: ew_tile2d<DA, DB, DO, -1>(q, v, p0, p1, k, lane); return;
+  }
+}
+#endif
+
+__device__ __forceinline__ void tile2d_dispatch(const ReqView& q, int v, float p0, float p1,
+                                                uint32_t k, int lane) {
+#ifndef GPUOS_JIT_LINK
+  const bool hasb = q.flags & RF_HAS_B;
+  if (hasb) {
+    if (q.dta == kF32 && q.dtb == kF32 && q.dto == kF32) return tile2d_ops<kF32, kF32, kF32>(q, v, p0, p1, k, lane);
+    if (q.dta == kF16 && q.dtb == kF32 && q.dto == kF32) return tile2d_ops<kF16, kF32, kF32>(q, v, p0, p1, k, lane);
+    if (q.dta == kBF16 && q.dtb == kBF16 && q.dto == kBF16) return tile2d_ops<kBF16, kBF16, kBF16>(q, v, p0, p1, k, lane);
+    if (q.dta == kF16 && q.dtb == kF16 && q.dto == kF16) return tile2d_ops<kF16, kF16, kF16>(q, v, p0, p1, k, lane);
+  }
+#endif
+  ew_tile2d<-1, -1, -1, -1>(q, v, p0, p1, k, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -722,6 +841,10 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
       if (ex.lane == 0) set_err(ex, ERR_BAD_OP);
       return;
     }
+    if (q.layout == EL_TILE2D) {
+      tile2d_dispatch(q, v, p0, p1, k, ex.lane);
+      return;
+    }
     const int64_t e0 = (int64_t)k * q.chunk;
     int64_t e1 = e0 + q.chunk;
     if (e1 > q.numel) e1 = q.numel;
@@ -756,6 +879,11 @@ __device__ __forceinline__ void finish_batch(const Exec& ex) {
   const uint64_t seq = ex.seq;
   const uint32_t err = atomicOr(&ex.st->err, 0u);
   const uint64_t word = (seq + 1) | ((uint64_t)(err & 0xffu) << 48);
+  if (ex.dur_ring) {
+    // device time of the batch: first CTA in -> this last chunk
+    const uint64_t nt0 = atomicAdd(reinterpret_cast<unsigned long long*>(&ex.st->nt0), 0ull);
+    ex.dur_ring[seq % kDoneRing] = nt0 ? globaltimer() - ~nt0 : 0ull;
+  }
   if (ex.done_dev) {
     st_release_gpu_u64(&ex.done_dev[seq % kDoneRing], word);
     st_release_sys_u64(&ex.done_ring[seq % kDoneRing], word);
@@ -769,7 +897,8 @@ __device__ __forceinline__ void finish_batch(const Exec& ex) {
 // worker) and its device-side counters.
 __device__ __forceinline__ Exec bind_batch(const uint8_t* payload, const BatchHdr& h,
                                            BatchState* st, volatile uint64_t* done_ring,
-                                           uint64_t* done_dev, uint64_t wait_limit_ns) {
+                                           uint64_t* done_dev, uint64_t wait_limit_ns,
+                                           volatile uint64_t* dur_ring = nullptr) {
   Exec ex;
   ex.base = payload;
   ex.st = st;
@@ -787,6 +916,7 @@ __device__ __forceinline__ Exec bind_batch(const uint8_t* payload, const BatchHd
   ex.wait_from = h.wait_from;
   ex.done_ring = done_ring;
   ex.done_dev = done_dev;
+  ex.dur_ring = dur_ring;
   ex.wait_limit_ns = wait_limit_ns;
   ex.lane = threadIdx.x & 31;
   return ex;

@@ -62,6 +62,9 @@ enum EwLayout : uint8_t {
   EL_CONTIG = 0,   // every operand contiguous over numel (or a scalar), out contiguous
   EL_ROW2D = 1,    // [rows, inner]; each operand: any row stride, inner stride 0 or 1
   EL_STRIDED = 2,  // general <= 8 dims through an extension record
+  EL_TILE2D = 3,   // [rows, inner], output inner stride 1, operands with any row and inner
+                   // strides (transposed views, [B,N] op [N] / [B,1] with N not a multiple
+                   // of 4); a chunk is `chunk` columns of every row (rows in nseg)
 };
 
 // reduction layouts: input seen as [rows, cols], reduce over cols
@@ -162,7 +165,11 @@ struct alignas(16) BatchState {
   uint32_t done;         // chunks finished
   uint32_t ctas_left;    // CTAs that left the batch
   uint32_t err;          // ErrBits
+  uint64_t nt0;          // ~(%globaltimer) of the first CTA to enter (atomicMax of the
+                         // complement: 0 means none yet)
+  uint64_t pad;
 };
+static_assert(sizeof(BatchState) == 32, "BatchState must stay 32 bytes");
 
 enum ErrBits : uint32_t {
   ERR_BAD_OP = 1,        // slot resolved to no variant (reference drops such tasks silently)
@@ -262,6 +269,7 @@ struct alignas(16) LeanHdr {
   uint64_t seq;
   uint64_t st;           // BatchState* of the batch (device)
   uint64_t done_ring;    // completion words (device view of mapped host memory)
+  uint64_t dur_ring;     // device time of each batch, ns (same)
   uint32_t nreq, nchunk;
   uint32_t flags;        // LeanFlags
   uint32_t pad;
@@ -285,6 +293,7 @@ struct WorkerArgs {
   DevCtrl* dctrl;                // device control block
   volatile uint64_t* done_ring;
   volatile uint64_t* retired_ring;
+  volatile uint64_t* dur_ring;   // device time of each batch (first CTA in -> last chunk), ns
   uint64_t start_seq;
   uint64_t wait_limit_ns;        // bound of every wait inside a batch
   uint64_t idle_ns;              // ingest: stop after this long without a batch

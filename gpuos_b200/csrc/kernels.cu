@@ -161,7 +161,9 @@ __device__ __forceinline__ void worker_loop(const WorkerArgs& w, CtaSmem* sm) {
     }
     __syncthreads();
     const Exec ex = bind_batch(payload, sm->hdr, &w.states[s % kDoneRing], w.done_ring,
-                               w.dctrl->done_dev, w.wait_limit_ns);
+                               w.dctrl->done_dev, w.wait_limit_ns, w.dur_ring);
+    if (threadIdx.x == 0)
+      atomicMax(reinterpret_cast<unsigned long long*>(&ex.st->nt0), ~globaltimer());
     if (threadIdx.x == 0 && (ex.flags & BF_AFTER_PREV)) wait_prev_batches(ex);
     __syncthreads();
     const uint32_t count = warp_batch(ex, gw, nproc * kWarpsPerCta, &sm->ext[threadIdx.x >> 5]);

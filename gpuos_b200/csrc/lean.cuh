@@ -12,16 +12,18 @@
 //   * warp g of W runs the contiguous chunk range [g n / W, (g + 1) n / W):
 //     the host sorts a batch's requests by operator, so the warps of an SM
 //     run one or two operator bodies;
-//   * a warp finds its first request by a binary search of the chunk prefix
-//     in parameter space and reads records from there: no staging copy of
-//     the batch, no granule table, no dependent global loads before the
+//   * the CTA copies the chunk prefix from parameter space into shared
+//     memory (one element per thread), each warp finds its first request by
+//     a binary search there and reads its records from parameter space: no
+//     staging copy of the batch, no granule table, no global load before the
 //     first data load;
 //   * programmatic dependent launch: a batch launches while the previous one
-//     drains.  It waits for the previous grid before touching memory when
-//     the host says so (LEAN_WAIT_FIRST: the first batch of a flush, or a
-//     hazard with an earlier batch of the same flush), lets the next batch
-//     launch once it runs, and waits for the previous grid before it exits,
-//     so that batches complete in stream order.
+//     drains and does its parameter-only set-up meanwhile.  It waits for the
+//     previous grid before touching global memory when the host says so
+//     (LEAN_WAIT_FIRST: the first batch of a flush, or a hazard with an
+//     earlier batch of the same flush), lets the next batch launch at once,
+//     and waits for the previous grid before it exits, so that batches
+//     complete in stream order.
 //   * completion: the last CTA posts the batch's completion word (seq + 1)
 //     to mapped host memory.
 #pragma once
@@ -116,9 +118,16 @@ __device__ __forceinline__ void lean_decode(LeanCur& u, const LeanBatch<N>& bt, 
 
 template <int N>
 __device__ __forceinline__ void lean_batch(const LeanBatch<N>& bt) {
+  __shared__ uint32_t s_cb[N + 1];
   const LeanHdr& h = bt.h;
-  if (h.flags & LEAN_WAIT_FIRST) gdc_wait();
   gdc_launch_dependents();
+  BatchState* st = reinterpret_cast<BatchState*>(h.st);
+  if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned long long*>(&st->nt0), ~globaltimer());
+  // the chunk prefix into shared memory, one element per thread: every warp
+  // then searches it there instead of through dependent parameter reads
+  const uint32_t nreq = h.nreq;
+  for (uint32_t i = threadIdx.x; i <= nreq; i += blockDim.x) s_cb[i] = bt.cb[i];
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   constexpr uint32_t kWarps = kLeanThreads / 32;
   const uint64_t W = (uint64_t)gridDim.x * kWarps;
@@ -126,41 +135,45 @@ __device__ __forceinline__ void lean_batch(const LeanBatch<N>& bt) {
   const uint32_t nchunk = h.nchunk;
   const uint32_t c0 = (uint32_t)(gw * nchunk / W);
   const uint32_t c1 = (uint32_t)((gw + 1) * nchunk / W);
-  if (c0 < c1) {
-    // the request holding chunk c0: cb[lo] <= c0 < cb[lo + 1]
-    uint32_t lo = 0, hi = h.nreq;
-    while (hi - lo > 1) {
-      const uint32_t mid = (lo + hi) >> 1;
-      if (bt.cb[mid] <= c0) lo = mid;
-      else hi = mid;
+  // the request holding chunk c0: s_cb[lo] <= c0 < s_cb[lo + 1]
+  uint32_t lo = 0, hi = nreq;
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (s_cb[mid] <= c0) lo = mid;
+    else hi = mid;
+  }
+  uint32_t r = lo;
+  LeanCur u;
+  lean_decode(u, bt, r);
+  // everything above reads parameters and shared memory only; memory the
+  // previous grid may write is touched from here on
+  if (h.flags & LEAN_WAIT_FIRST) gdc_wait();
+  uint32_t rbase = s_cb[r], rend = s_cb[r + 1];
+  for (uint32_t c = c0; c < c1; ++c) {
+    if (c >= rend) {
+      do {
+        ++r;
+        rbase = rend;
+        rend = s_cb[r + 1];
+      } while (c >= rend);
+      lean_decode(u, bt, r);
     }
-    uint32_t r = lo;
-    LeanCur u;
-    lean_decode(u, bt, r);
-    uint32_t rbase = bt.cb[r], rend = bt.cb[r + 1];
-    for (uint32_t c = c0; c < c1; ++c) {
-      if (c >= rend) {
-        do {
-          ++r;
-          rbase = rend;
-          rend = bt.cb[r + 1];
-        } while (c >= rend);
-        lean_decode(u, bt, r);
-      }
-      const uint32_t e0 = (c - rbase) * u.chunk;
-      const uint32_t n = min(u.chunk, u.numel - e0);
-      lean_dispatch(u, bt, e0, n, lane);
-    }
+    const uint32_t e0 = (c - rbase) * u.chunk;
+    const uint32_t n = min(u.chunk, u.numel - e0);
+    lean_dispatch(u, bt, e0, n, lane);
   }
   // completion: every CTA releases its stores, the last one posts the word
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    BatchState* st = reinterpret_cast<BatchState*>(h.st);
     const uint32_t left = atomicAdd(&st->ctas_left, 1u) + 1u;
     if (left == gridDim.x) {
       __threadfence();
+      const uint64_t nt0 = *reinterpret_cast<volatile uint64_t*>(&st->nt0);
+      st->nt0 = 0ull;
       st->ctas_left = 0u;
+      reinterpret_cast<volatile uint64_t*>(h.dur_ring)[h.seq % kDoneRing] =
+          nt0 ? globaltimer() - ~nt0 : 0ull;
       volatile uint64_t* dr = reinterpret_cast<volatile uint64_t*>(h.done_ring);
       st_release_sys_u64(&dr[h.seq % kDoneRing], h.seq + 1);
     }

@@ -394,7 +394,7 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
 
   // host control block + rings
   const size_t hb = align_up(sizeof(HostCtrl), 256) + align_up(sizeof(Pub) * kDoneRing, 256) +
-                    2 * sizeof(uint64_t) * kDoneRing + 256;
+                    3 * sizeof(uint64_t) * kDoneRing + 256;
   GCU(cudaHostAlloc(reinterpret_cast<void**>(&hostblk_), hb, cudaHostAllocMapped));
   std::memset(hostblk_, 0, hb);
   GCU(cudaHostGetDevicePointer(reinterpret_cast<void**>(&hostblk_dev_), hostblk_, 0));
@@ -407,6 +407,9 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   o += sizeof(uint64_t) * kDoneRing;
   retired_ring_ = reinterpret_cast<volatile uint64_t*>(hostblk_ + o);
   o += sizeof(uint64_t) * kDoneRing;
+  dur_ring_ = reinterpret_cast<volatile uint64_t*>(hostblk_ + o);
+  o += sizeof(uint64_t) * kDoneRing;
+  stop_src_ = hostblk_ + o;
   *reinterpret_cast<uint64_t*>(hostblk_ + o) = UINT64_MAX;  // source of the stop_at reset
 
   GCU(cudaMalloc(reinterpret_cast<void**>(&dctrl_), sizeof(DevCtrl)));
@@ -529,6 +532,11 @@ void build_ew(Pending& p, int op, bool is_slot, float p0, float p1,
                      opnd_vec(a_sc, q.a, q.sa_row, q.sa_in, ea) &&
                      (!b || opnd_vec(b_sc, q.b, q.sb_row, q.sb_in, eb));
     if (vec) q.flags |= RF_VEC;
+    if (!vec && m == 2 && R <= 1024 && numel < (1ll << 31)) {
+      // 2-D tiles: chunks of whole columns, no division per element
+      q.layout = EL_TILE2D;
+      q.nseg = (uint32_t)R;
+    }
     if (numel >= (1ll << 31) || N >= (1ll << 31)) {
       q.flags |= RF_BIG;
     } else {
@@ -790,6 +798,7 @@ void Executor::reclaim() {
           if (err_seq_ == UINT64_MAX) err_seq_ = done_wm_;
           err_bits_ |= e;
         }
+        dev_ns_ += dur_ring_[done_wm_ % kDoneRing];
         ++done_wm_;
         continue;
       }
@@ -821,6 +830,7 @@ void Executor::reclaim() {
       if (err_seq_ == UINT64_MAX) err_seq_ = done_wm_;
       err_bits_ |= e;
     }
+    dev_ns_ += dur_ring_[done_wm_ % kDoneRing];
     ++done_wm_;
   }
   while (retired_wm_ < next_seq_) {
@@ -953,7 +963,8 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   // with per-row operands and 4 for the general body (from per-chunk timings).
   auto ew_cost = [](const Pending& p, int v) -> uint64_t {
     uint64_t w = (uint64_t)chunk_weight(v);
-    if (!(p.r.flags & RF_VEC) || p.r.layout == EL_STRIDED) w *= 4;
+    if (p.r.layout == EL_TILE2D) w *= 2;
+    else if (!(p.r.flags & RF_VEC) || p.r.layout == EL_STRIDED) w *= 4;
     else if (p.r.layout == EL_ROW2D) w *= 2;
     return w;
   };
@@ -1010,6 +1021,16 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     Pending& p = reqs[i + r];
     if (p.r.kind != RK_EW) continue;
     uint64_t c = std::max<uint64_t>(128, (staged ? stage_ce[r] : ce) >> cost_log2[r]);
+    if (p.r.layout == EL_TILE2D) {
+      // whole columns: c elements make c / rows columns, a multiple of 32
+      const uint64_t R = std::max<uint32_t>(1u, p.r.nseg), N = (uint64_t)p.r.inner;
+      uint64_t cols = align_up(std::max<uint64_t>(1, c / R), 32);
+      const uint64_t k = (N + cols - 1) / cols;
+      cols = align_up((N + k - 1) / k, 32);
+      p.r.chunk = (uint32_t)cols;
+      p.nchunk = (uint32_t)((N + cols - 1) / cols);
+      continue;
+    }
     if (p.r.layout == EL_STRIDED) c = std::min<uint64_t>(c, 2048);
     // equal chunks (a multiple of 4 elements, as the vector path needs)
     const uint64_t numel = (uint64_t)p.r.numel;
@@ -1172,6 +1193,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   next_seq_ = seq + 1;
 
   if (opt_.mode == GPUOS_MODE_PERSISTENT) {
+    dur_ring_[seq % kDoneRing] = 0;
     Pub& pb = pub_[seq % kDoneRing];
     pb.seq = seq;
     pb.off = (uint32_t)aoff;
@@ -1265,7 +1287,8 @@ void effective_params(const Tables& tab, const Req& q, float* p0, float* p1) {
 }
 
 template <int N>
-void fill_lean(uint8_t* buf, uint64_t seq, uint64_t st, uint64_t done_ring, uint32_t flags,
+void fill_lean(uint8_t* buf, uint64_t seq, uint64_t st, uint64_t done_ring, uint64_t dur_ring,
+               uint32_t flags,
                const std::vector<Pending>& reqs, size_t i, uint32_t n, const std::vector<int>& var,
                const std::vector<uint32_t>& order, uint64_t nchunk, const Tables& tab) {
   LeanBatch<N>* b = reinterpret_cast<LeanBatch<N>*>(buf);
@@ -1273,6 +1296,7 @@ void fill_lean(uint8_t* buf, uint64_t seq, uint64_t st, uint64_t done_ring, uint
   b->h.seq = seq;
   b->h.st = st;
   b->h.done_ring = done_ring;
+  b->h.dur_ring = dur_ring;
   b->h.nreq = n;
   b->h.nchunk = (uint32_t)nchunk;
   b->h.flags = flags;
@@ -1363,11 +1387,14 @@ bool Executor::publish_lean(std::unique_lock<std::mutex>& lk, std::vector<Pendin
   const uint64_t st = reinterpret_cast<uint64_t>(states_ + seq % kDoneRing);
   const uint64_t dr = reinterpret_cast<uint64_t>(
       hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));
+  const uint64_t du = reinterpret_cast<uint64_t>(
+      hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(dur_ring_) - hostblk_));
   const uint32_t flags = wf ? LEAN_WAIT_FIRST : 0u;
   uint8_t* buf = lean_buf_.data();
-  if (cls == 0) fill_lean<32>(buf, seq, st, dr, flags, reqs, i, n, var, order, nchunk, tab_);
-  else if (cls == 1) fill_lean<128>(buf, seq, st, dr, flags, reqs, i, n, var, order, nchunk, tab_);
-  else fill_lean<kLeanMaxReq>(buf, seq, st, dr, flags, reqs, i, n, var, order, nchunk, tab_);
+  if (cls == 0) fill_lean<32>(buf, seq, st, dr, du, flags, reqs, i, n, var, order, nchunk, tab_);
+  else if (cls == 1) fill_lean<128>(buf, seq, st, dr, du, flags, reqs, i, n, var, order, nchunk, tab_);
+  else fill_lean<kLeanMaxReq>(buf, seq, st, dr, du, flags, reqs, i, n, var, order, nchunk, tab_);
+  dur_ring_[seq % kDoneRing] = 0;
   DeviceGuard g(device_);
   if (have_last_stream_ && stream != last_stream_ && done_wm_ < seq) {
     GCU(cudaEventRecord(last_event_, last_stream_));
@@ -1583,10 +1610,7 @@ void Executor::launch_worker_locked(uint64_t start) {
   hctrl_->exit_reason = 0u;
   hctrl_->idle_ns = idle_ns_;
   std::atomic_thread_fence(std::memory_order_seq_cst);
-  const uint8_t* stop_src = hostblk_ + align_up(sizeof(HostCtrl), 256) +
-                            align_up(sizeof(Pub) * kDoneRing, 256) +
-                            2 * sizeof(uint64_t) * kDoneRing;
-  GCU(cudaMemcpyAsync(&dctrl_->stop_at, stop_src, sizeof(uint64_t), cudaMemcpyHostToDevice,
+  GCU(cudaMemcpyAsync(&dctrl_->stop_at, stop_src_, sizeof(uint64_t), cudaMemcpyHostToDevice,
                       s_worker_));
   WorkerArgs w;
   w.ring = ring_;
@@ -1600,6 +1624,8 @@ void Executor::launch_worker_locked(uint64_t start) {
       hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));
   w.retired_ring = reinterpret_cast<volatile uint64_t*>(
       hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(retired_ring_) - hostblk_));
+  w.dur_ring = reinterpret_cast<volatile uint64_t*>(
+      hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(dur_ring_) - hostblk_));
   w.start_seq = start;
   w.wait_limit_ns = wait_limit_ns_;
   w.idle_ns = idle_ns_;

@@ -178,6 +178,8 @@ class Executor {
   Pub* pub_ = nullptr;
   volatile uint64_t* done_ring_ = nullptr;
   volatile uint64_t* retired_ring_ = nullptr;
+  volatile uint64_t* dur_ring_ = nullptr;  // device ns of each completed batch (worker, lean)
+  uint8_t* stop_src_ = nullptr;            // a UINT64_MAX word: source of the stop_at reset
   uint8_t* hostblk_dev_ = nullptr;
 
   // device memory

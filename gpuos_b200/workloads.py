@@ -152,6 +152,9 @@ class Stream:
         (in_lo, in_hi, out_lo, out_hi) of the two slabs its tensors cover.
         Slabs are allocated in request order, so the groups' ranges follow
         one another."""
+        return self.batch_spans_of(self.requests)
+
+    def batch_spans_of(self, requests):
         def span(t: TensorSpec):
             n = 1
             for sz, st in zip(t.shape, t.strides):
@@ -159,10 +162,10 @@ class Stream:
             return t.off, t.off + n * _ESZ[t.dtype]
         res = []
         fe = self.flush_every
-        for i in range(0, len(self.requests), fe):
+        for i in range(0, len(requests), fe):
             ilo = olo = 1 << 62
             ihi = ohi = 0
-            for r in self.requests[i:i + fe]:
+            for r in requests[i:i + fe]:
                 for t in (r.a, r.b):
                     if t is not None:
                         lo, hi = span(t)
@@ -172,11 +175,42 @@ class Stream:
             res.append((ilo, ihi, olo, ohi))
         return res
 
+    def head(self, n: int) -> "Stream":
+        """The stream of its first n requests, with the slabs cut to what those
+        requests use (slabs are allocated in request order)."""
+        reqs = self.requests[:n]
+        spans = self.batch_spans_of(reqs)
+        in_end = max(s[1] for s in spans) if reqs else 0
+        out_end = max(s[3] for s in spans) if reqs else 0
+        host = self.host_in[:in_end] if self.host_in is not None else None
+        return Stream(self.name, reqs, in_end, out_end, host, self.flush_every, dict(self.meta))
+
     def device_buffers(self, device, pin=False):
-        """(inputs, outputs) byte slabs on `device` with the inputs copied."""
-        din = self.host_in.to(device)
+        """(inputs, outputs) byte slabs on `device` with the inputs copied (or,
+        for a stream built without host values, drawn on the device)."""
         dout = torch.zeros(self.out_bytes, dtype=torch.uint8, device=device)
+        if self.host_in is None:
+            return self.device_inputs(device), dout
+        din = self.host_in.to(device)
         return din, dout
+
+    def device_inputs(self, device, seed=0):
+        """The input slab drawn on the device: every input view gets the
+        stream's value distribution (meta["dist"]: "normal" or "u2"), from a
+        device generator.  For timing runs of streams too large to draw on
+        the host; the values differ from the host-built stream's."""
+        din = torch.empty(self.in_bytes, dtype=torch.uint8, device=device)
+        g = torch.Generator(device=device).manual_seed(seed)
+        dist = self.meta.get("dist", "normal")
+        for r in self.requests:
+            for t in (r.a, r.b):
+                if t is None:
+                    continue
+                v = t.view(din)
+                x = torch.randn(v.shape, generator=g, device=device) if dist == "normal" else \
+                    torch.rand(v.shape, generator=g, device=device) * 4 - 2
+                v.copy_(x)
+        return din
 
     def views(self, din, dout):
         """per request (a, b, out) tensor views into the two slabs"""
@@ -259,7 +293,7 @@ BCAST_OPS = [("add", "add"), ("sub", "sub"), ("mul", "mul"), ("div", "div0"),
              ("maximum", "maximum"), ("minimum", "minimum")]
 
 
-def broadcast_mixed(n_req=8192, seed=0, flush_every=512) -> Stream:
+def broadcast_mixed(n_req=8192, seed=0, flush_every=512, fill=True) -> Stream:
     g = torch.Generator().manual_seed(seed)
     si, so = Slab(), Slab()
     reqs = []
@@ -282,6 +316,9 @@ def broadcast_mixed(n_req=8192, seed=0, flush_every=512) -> Stream:
             b = _contig(si.alloc(N * _ESZ[db]), db, (N,))
         o = _contig(so.alloc(B * N * _ESZ[dout]), dout, (B, N))
         reqs.append(Request(sop, op, 0.0, 0.0, a, b, o))
+    if not fill:
+        return Stream("broadcast_mixed", reqs, si.size, so.size, None, flush_every=flush_every,
+                      meta={"requests": n_req, "dist": "u2", "dtype": "f32/f16/bf16"})
     buf = torch.empty(si.size, dtype=torch.uint8)
     for r in reqs:
         B, N = r.out.shape
@@ -292,10 +329,10 @@ def broadcast_mixed(n_req=8192, seed=0, flush_every=512) -> Stream:
             y = torch.where(y.abs() < 0.05, torch.full_like(y, 0.5), y)
         _fill(buf, r.b, y.to(r.b.dtype))
     return Stream("broadcast_mixed", reqs, si.size, so.size, buf, flush_every=flush_every,
-                  meta={"requests": n_req})
+                  meta={"requests": n_req, "dist": "u2", "dtype": "f32/f16/bf16"})
 
 
-def lastdim_reduce(n_req=4096, seed=0, flush_every=512, max_elems=1 << 24) -> Stream:
+def lastdim_reduce(n_req=4096, seed=0, flush_every=512, max_elems=1 << 24, fill=True) -> Stream:
     g = torch.Generator().manual_seed(seed)
     si, so = Slab(), Slab()
     reqs = []
@@ -313,12 +350,15 @@ def lastdim_reduce(n_req=4096, seed=0, flush_every=512, max_elems=1 << 24) -> St
         o = _contig(so.alloc(R * _ESZ[dt]), dt, (R, 1) if keep else (R,))
         op = "mean" if mean else "sum"
         reqs.append(Request(op, op, 0.0, 0.0, x, None, o, kind="reduce", axes=(1,), keepdim=keep))
+    if not fill:
+        return Stream("lastdim_reduce", reqs, si.size, so.size, None, flush_every=flush_every,
+                      meta={"requests": n_req, "dist": "normal", "dtype": "f32/bf16"})
     buf = torch.empty(si.size, dtype=torch.uint8)
     for r in reqs:
         R, C = r.a.shape
         _fill(buf, r.a, torch.randn(R * C, generator=g).to(r.a.dtype))
     return Stream("lastdim_reduce", reqs, si.size, so.size, buf, flush_every=flush_every,
-                  meta={"requests": n_req})
+                  meta={"requests": n_req, "dist": "normal", "dtype": "f32/bf16"})
 
 
 STREAMS = {

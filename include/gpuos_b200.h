@@ -85,7 +85,8 @@ typedef struct gpuos_stats {
   uint64_t pending;     /* requests waiting for the next flush */
   uint64_t errors;      /* device-reported request errors */
   uint64_t relaunches;  /* persistent worker launches */
-  uint64_t dev_ns;      /* device time of completed batches (first claim -> last chunk) */
+  uint64_t dev_ns;      /* device time of completed batches, ns: first CTA in -> last chunk
+                           (persistent worker and lean batches) */
   uint64_t lean;        /* stream-mode batches run by the lean kernel (parameters only) */
   int32_t capacity;
   int32_t max_batch;

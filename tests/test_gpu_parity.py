@@ -716,10 +716,12 @@ def test_custom_expression_ordering_and_hot_swap(mode):
 # a SiLU-style gate (sigmoid, mul) on [b, 11008]; several layers in ONE flush,
 # so every step depends on the one before.
 # ---------------------------------------------------------------------------
+@pytest.mark.parametrize("B", [1, 8, 64])
 @pytest.mark.parametrize("mode", MODES, ids=MODE_IDS)
-def test_decode_chain_bf16(mode):
+def test_decode_chain_bf16(mode, B):
+    """All 32 layers of the decode configuration, one flush."""
     bf = torch.bfloat16
-    B, H, F, L = 8, 4096, 11008, 3
+    H, F, L = 4096, 11008, 32
     g = torch.Generator().manual_seed(91)
 
     def normal(*shape):

@@ -102,7 +102,9 @@ def test_plan_broadcast_row_col_scalar():
 def test_plan_transposed_and_strided():
     At = torch.randn(64, 8).t()
     p = plan("add", At, torch.randn(64), torch.empty(8, 64))
-    assert p["layout"] == 1 and p["sa_row"] == 1 and p["sa_in"] == 8 and not p["flags"] & 2
+    # a transposed operand: 2-D tiles of whole columns (rows in nseg)
+    assert p["layout"] == 3 and p["sa_row"] == 1 and p["sa_in"] == 8 and not p["flags"] & 2
+    assert p["nseg"] == 8 and p["inner"] == 64
     x = torch.randn(4, 5, 6, 7).permute(2, 0, 3, 1)
     p = plan("add", x, x, torch.empty(6, 4, 7, 5))
     assert p["layout"] == 1 or p["layout"] == 2
@@ -167,7 +169,7 @@ def _desc(shape, strides, addr=1 << 20):
 
 
 def _magic(N):
-    """fdiv constants the runtime stores in the ROW2D record of a [2, N] op [N]
+    """fdiv constants the runtime stores in the 2-D record of a [2, N] op [N]
     request (descriptors only: planning never touches the memory)."""
     import ctypes
     a, b, o = _desc((2, N), (N, 1)), _desc((N,), (1,)), _desc((2, N), (N, 1), 1 << 40)
@@ -175,7 +177,7 @@ def _magic(N):
     C.check(C.lib().gpuos_plan_elementwise(C.variant("add"), 0.0, 0.0, ctypes.byref(a),
                                            ctypes.byref(b), ctypes.byref(o), ctypes.byref(p)))
     r = C.decode_record(bytes(p.record))
-    assert r["layout"] == 1 and r["inner"] == N
+    assert r["layout"] in (1, 3) and r["inner"] == N   # ROW2D, or 2-D tiles when N % 4 != 0
     return r["fdiv_m"], r["fdiv_s"]
 
 
