@@ -210,6 +210,15 @@ def dist_setup(n_gpus):
         import datetime
 
         import torch.distributed as dist
+        # each rank's host thread submits its own stream: give every rank its
+        # own slice of the host cores so that ranks do not share one
+        try:
+            cores = sorted(os.sched_getaffinity(0))
+            k = max(1, len(cores) // max(1, int(os.environ.get("LOCAL_WORLD_SIZE", world))))
+            mine = cores[local * k:(local + 1) * k] or cores
+            os.sched_setaffinity(0, mine)
+        except (AttributeError, OSError):
+            pass
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
@@ -227,6 +236,18 @@ def allmax(x: float, world: int) -> float:
     t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def allgather(x: float, world: int) -> list:
+    """x from every rank, in rank order."""
+    if world == 1:
+        return [x]
+    import torch.distributed as dist
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
 
 
 def whole_job_rate(units_per_rank: int, seconds: float, world: int) -> float:
@@ -535,6 +556,52 @@ def decode_chain(ext, dev, batches=(1, 8, 64), layers=32, steps=20, warmup=3):
     return out
 
 
+def persistent_leg(ext, stream, din, dout, steps, world):
+    """The same stream through the persistent worker (gpuos_ext.init(...,
+    mode="persistent")): requests/s timed as the main run is, and the
+    worker's own device time per batch (stats dev_ns: first CTA to enter a
+    batch -> its last chunk, from %globaltimer stamps) with the roofline of
+    that time."""
+    from gpuos_b200 import workloads as W
+    peak, peak_kind = peaks()
+    ext.init(8192, 256, mode="persistent")
+    try:
+        calls = W.Submitter(ext).prepare(stream, stream.views(din, dout))
+        fe = stream.flush_every
+        for _ in range(2):
+            run_step(ext, calls, fe)
+        cur = torch.cuda.current_stream()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        q0 = ext.peek_queue()
+        ev0.record(cur)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            run_step(ext, calls, fe)
+        ev1.record(cur)
+        ev1.synchronize()
+        wall = time.perf_counter() - t0
+        q1 = ext.peek_queue()
+    finally:
+        ext.shutdown()
+    t_step = allmax(max(ev0.elapsed_time(ev1) / 1e3, wall) / steps, world)
+    batches = q1["processed"] - q0["processed"]
+    dev_s = (q1["dev_ns"] - q0["dev_ns"]) / 1e9
+    per_batch = dev_s / max(1, batches)
+    bytes_per_batch = stream.algo_bytes * steps / max(1, batches)
+    achieved = bytes_per_batch / per_batch / 1e9 if per_batch > 0 else None
+    return {"value": round(world * len(stream.requests) / t_step, 1), "unit": "requests/s",
+            "ms_per_step": round(t_step * 1e3, 3), "batches": int(batches),
+            "device_us_per_batch": round(per_batch * 1e6, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1) if achieved else None,
+                         "peak": peak, "unit": "GB/s", "peak_kind": peak_kind,
+                         "frac": round(achieved / peak, 4) if achieved else None,
+                         "kernel": "gpuos_worker_kernel",
+                         "how": "device time per batch from the worker's %globaltimer stamps "
+                                "(first CTA in -> last chunk), not an ncu capture"},
+            "relaunches": int(q1["relaunches"] - q0["relaunches"])}
+
+
 def flush_latency(ext, dev, reps=400):
     """p50 of flush(sync=True) for one 4096-element add, and for the
     1024 x 4096 add/mul batch."""
@@ -689,7 +756,8 @@ def bench_ours(args, world, rank, local):
     q1 = ext.peek_queue()
     ev_s = ev0.elapsed_time(ev1) / 1e3
     host_out = dout.cpu()  # the last timed step's outputs, checked below
-    t_step = allmax(max(ev_s, wall) / args.steps, world)  # per step, slowest rank
+    per_rank_ms = [round(v * 1e3, 3) for v in allgather(max(ev_s, wall) / args.steps, world)]
+    t_step = max(per_rank_ms) / 1e3  # per step, slowest rank
     torch.cuda.synchronize()
     clk = clocks.stop()
     batches = q1["tail"] - q0["tail"]
@@ -719,6 +787,8 @@ def bench_ours(args, world, rank, local):
     lat = flush_latency(ext, dev) if rank == 0 else None
     chain = decode_chain(ext, dev) if rank == 0 else None
     ext.shutdown()
+    pers = persistent_leg(ext, stream, din, dout, max(2, min(args.steps, 5)), world) \
+        if args.mode == "stream" else None
 
     peak, peak_kind = peaks()
     rsteps = max(2, min(args.steps, 5))
@@ -773,12 +843,14 @@ def bench_ours(args, world, rank, local):
                    "l2": f"inputs {stream.in_bytes / 1e9:.2f} GB per step > 126 MB L2",
                    "parallelism": f"{world} independent executors (one per GPU)"},
         "gbs_whole_step": round(world * stream.algo_bytes / t_step / 1e9, 1),
+        "per_rank_ms_per_step": per_rank_ms,
         "e2e": {"value": round(world * n_req / t_e2e, 1), "unit": "requests/s",
                 "h2d_bytes_per_step": stream.in_bytes, "d2h_bytes_per_step": stream.out_bytes},
         "roofline": roof,
         "cpu_baseline": cpu,
         "flush_p50_us": lat,
         "decode_chain": chain,
+        "persistent": pers,
         "check": check,
         "gpu_launches": int(launches * world),
         "clocks": clk,

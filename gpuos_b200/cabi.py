@@ -78,6 +78,8 @@ SIGNATURES = {
     "gpuos_set_debug_level": (ctypes.c_int32, [_VP, ctypes.c_int32]),
     "gpuos_worker_alive": (ctypes.c_int32, [_VP]),
     "gpuos_debug_stall_next_batch": (ctypes.c_int32, [_VP]),
+    "gpu_set_op_table_async": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_uint64, _VP]),
+    "gpu_set_alias_async": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_int32, _VP]),
     "gpuos_plan_elementwise": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_float, ctypes.c_float,
                                                 P(Tensor), P(Tensor), P(Tensor), P(Plan)]),
     "gpuos_plan_reduce": (ctypes.c_int32, [ctypes.c_int32, P(Tensor), P(Tensor), P(ctypes.c_int32),

@@ -32,7 +32,18 @@ static constexpr int kWarpsPerCta = 8;
 static constexpr int kCtaThreads = 32 * kWarpsPerCta;
 static constexpr int kMinCtasPerSm = 2;
 
+// Stage waits of one CTA share one poller: the warp that takes `poller`
+// reads the batch's done counter (acquire) and leaves the largest value seen
+// in `seen`; the CTA's other waiting warps watch `seen` in shared memory, so a
+// stage hop costs at most one poll round trip and the counter sees one poller
+// per CTA instead of one per warp.  Both are zero when a batch starts.
+struct StageSync {
+  uint32_t seen;
+  int32_t poller;
+};
+
 struct CtaSmem {
+  StageSync ss;              // stage waits (batches with stage barriers)
   ExtRec ext[kWarpsPerCta];  // per warp: the strided request's dims and strides
   BatchHdr hdr;              // persistent worker: the current batch's header
   uint32_t chunks;           // chunks this CTA finished in the current batch
@@ -63,6 +74,22 @@ __device__ __forceinline__ void decode(Cur& cur, const Exec& ex, const Req* rec,
   cur.v = q.op == kOpNone ? V_NONE : q.op;
   cur.p0 = q.p0;
   cur.p1 = q.p1;
+  if ((q.flags & RF_SLOT) && ex.tab) {
+    // the persistent worker resolves a slot when it starts the request:
+    // alias, then the physical slot's operator and parameters, with acquire
+    // loads (the reference's g_op_alias -> g_op_table read,
+    // src/persistent_kernel.cu:168-175), so a hot swap reaches batches that
+    // are published but not yet started
+    const int phys = q.op < kMaxSlots ? ld_acquire_s32(&ex.tab->alias[q.op]) : -1;
+    if (phys >= 0 && phys < kMaxSlots) {
+      const SlotEntry* e = &ex.tab->slot[phys];
+      cur.v = ld_acquire_s32(&e->variant);
+      cur.p0 = __int_as_float(ld_acquire_s32(reinterpret_cast<const int32_t*>(&e->p0)));
+      cur.p1 = __int_as_float(ld_acquire_s32(reinterpret_cast<const int32_t*>(&e->p1)));
+    } else {
+      cur.v = V_NONE;
+    }
+  }
   cur.vec = q.kind == RK_EW && (q.flags & RF_VEC) && q.layout != EL_STRIDED && ew_known(cur.v);
   if (cur.vec) {
     cur.u = vec_view(q);
@@ -97,7 +124,7 @@ __device__ __forceinline__ void run_chunk(const Exec& ex, Cur& cur, uint32_t k,
 // One warp's share of a batch: warp gw of W.  Returns the chunks it ran that
 // are still to be counted (all of them, unless the batch counts chunk by chunk).
 __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint32_t W,
-                                               ExtRec* xs) {
+                                               ExtRec* xs, StageSync* ss) {
   const int lane = ex.lane;
   const uint32_t nchunk = ex.nchunk;
   const bool staged = ex.flags & BF_STAGED;
@@ -164,20 +191,31 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
         const uint32_t w = __ldcg(ex.req_wait + r);
         if (w > waited) {
           // every chunk of the earlier stages must be done first
-          if (lane == 0 && ld_acquire_u32(&ex.st->done) < w) {
-            // exponential back-off: thousands of warps may wait on this one
-            // counter, and their polls would queue the increments of the
-            // chunks they wait for
-            const uint64_t t0 = globaltimer();
-            unsigned ns = 64;
-            while (ld_acquire_u32(&ex.st->done) < w) {
-              __nanosleep(ns);
-              if (ns < 1024) ns <<= 1;
-              if (globaltimer() - t0 > ex.wait_limit_ns) {
-                atomicOr(&ex.st->err, ERR_STAGE_TIMEOUT);
-                break;
+          if (lane == 0) {
+            volatile uint32_t* seen = &ss->seen;
+            if (*seen < w) {
+              const uint64_t t0 = globaltimer();
+              while (true) {
+                if (atomicCAS(&ss->poller, 0, 1) == 0) {
+                  // this warp polls for the CTA
+                  const uint32_t d = ld_acquire_u32(&ex.st->done);
+                  __threadfence_block();
+                  atomicMax(&ss->seen, d);
+                  atomicExch(&ss->poller, 0);
+                  if (d >= w) break;
+                  __nanosleep(32);
+                } else {
+                  __nanosleep(32);
+                }
+                if (*seen >= w) break;
+                if (globaltimer() - t0 > ex.wait_limit_ns) {
+                  atomicOr(&ex.st->err, ERR_STAGE_TIMEOUT);
+                  break;
+                }
               }
             }
+            // order this warp's loads after the acquire another warp may have made
+            __threadfence_block();
           }
           waited = w;
           __syncwarp();

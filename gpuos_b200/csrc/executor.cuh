@@ -39,6 +39,12 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+__device__ __forceinline__ int32_t ld_acquire_s32(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -158,6 +164,8 @@ struct Exec {
   volatile uint64_t* done_ring; // completion words in mapped host memory
   uint64_t* done_dev;           // device copy of the completion words (worker only)
   volatile uint64_t* dur_ring;  // device time of each batch (mapped host memory), or null
+  const Tables* tab;            // device jump table (persistent worker), or null: records
+                                // then carry resolved operators
   uint64_t wait_limit_ns;
   uint64_t seq;                 // batch sequence number
   uint64_t wait_from;           // BF_AFTER_PREV: batches [wait_from, seq) first
@@ -657,29 +665,53 @@ __device__ __forceinline__ void red_span_scalar(const ReqView& q, int64_t base, 
   }
 }
 
-// The same over groups of 4 aligned elements: lane i of the group adds groups
-// starting at c + 4 i, c + 4 (i + stride), ... up to c4 (a multiple of 4
-// elements past c); kRedU / 2 groups in flight per lane.
-__device__ __forceinline__ void red_span_vec(const ReqView& q, int64_t base, int64_t c, int64_t c4,
+// The same over 16-byte groups (4 fp32 or 8 fp16 / bf16 elements) starting
+// at c + GE i, c + GE (i + stride), ... up to cg (a multiple of GE elements
+// past c, GE = 16 / element size); kRedVU groups in flight per lane.
+static constexpr int kRedVU = 8;
+
+__device__ __forceinline__ void add16(uint4 w, int dt, float& acc0, float& acc1) {
+  if (dt == kF32) {
+    acc0 += __uint_as_float(w.x) + __uint_as_float(w.z);
+    acc1 += __uint_as_float(w.y) + __uint_as_float(w.w);
+    return;
+  }
+  float v[8];
+  if (dt == kF16) {
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
+      v[2 * k] = f.x;
+      v[2 * k + 1] = f.y;
+    }
+  } else {
+    bf2_to_f(w.x, v[0], v[1]);
+    bf2_to_f(w.y, v[2], v[3]);
+    bf2_to_f(w.z, v[4], v[5]);
+    bf2_to_f(w.w, v[6], v[7]);
+  }
+  acc0 += (v[0] + v[2]) + (v[4] + v[6]);
+  acc1 += (v[1] + v[3]) + (v[5] + v[7]);
+}
+
+__device__ __forceinline__ void red_span_vec(const ReqView& q, int64_t base, int64_t c, int64_t cg,
                                              int stride, float& acc0, float& acc1) {
-  constexpr int U = kRedU / 2;
+  const int GE = q.dta == kF32 ? 4 : 8;
+  const int64_t step = (int64_t)GE * stride;
+  const uint8_t* p = reinterpret_cast<const uint8_t*>(q.a);
+  const int es = q.dta == kF32 ? 4 : 2;
 #pragma unroll 1
-  for (; c < c4; c += 4 * (int64_t)stride * U) {
-    uint4 w[U];
+  for (; c < cg; c += step * kRedVU) {
+    uint4 w[kRedVU];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
+    for (int u = 0; u < kRedVU; ++u) {
       w[u] = make_uint4(0u, 0u, 0u, 0u);
-      if (c + 4 * (int64_t)stride * u < c4) w[u] = ld4_raw(q.a, q.dta, base + c + 4 * (int64_t)stride * u);
+      if (c + step * u < cg) w[u] = *reinterpret_cast<const uint4*>(p + (base + c + step * u) * es);
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (c + 4 * (int64_t)stride * u < c4) {
-        float v[4];
-        cvt4(w[u], q.dta, v);
-        acc0 += v[0] + v[2];
-        acc1 += v[1] + v[3];
-      }
-    }
+    for (int u = 0; u < kRedVU; ++u)
+      if (c + step * u < cg) add16(w[u], q.dta, acc0, acc1);
   }
 }
 
@@ -701,9 +733,10 @@ __device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool 
       if (valid) {
         const int64_t base = r * q.sa_row;
         if (vec) {
-          const int64_t C4 = C & ~(int64_t)3;
-          red_span_vec(q, base, 4 * (int64_t)li, C4, G, acc0, acc1);
-          red_span_scalar(q, base, C4 + li, C, G, acc0, acc1);
+          const int GE = q.dta == kF32 ? 4 : 8;
+          const int64_t CG = C & ~(int64_t)(GE - 1);
+          red_span_vec(q, base, (int64_t)GE * li, CG, G, acc0, acc1);
+          red_span_scalar(q, base, CG + li, C, G, acc0, acc1);
         } else {
           red_span_scalar(q, base, li, C, G, acc0, acc1);
         }
@@ -724,9 +757,10 @@ __device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool 
   const int64_t base = r * q.sa_row;
   float acc0 = 0.f, acc1 = 0.f;
   if (vec) {  // c0 is a multiple of 8 (chunk is), c1 may end ragged on the last segment
-    const int64_t c4 = c0 + ((c1 - c0) & ~(int64_t)3);
-    red_span_vec(q, base, c0 + 4 * lane, c4, 32, acc0, acc1);
-    red_span_scalar(q, base, c4 + lane, c1, 32, acc0, acc1);
+    const int GE = q.dta == kF32 ? 4 : 8;
+    const int64_t cg = c0 + ((c1 - c0) & ~(int64_t)(GE - 1));
+    red_span_vec(q, base, c0 + (int64_t)GE * lane, cg, 32, acc0, acc1);
+    red_span_scalar(q, base, cg + lane, c1, 32, acc0, acc1);
   } else {
     red_span_scalar(q, base, c0 + lane, c1, 32, acc0, acc1);
   }
@@ -798,6 +832,91 @@ __device__ __forceinline__ void red_cols(const Exec& ex, const ReqView& q, bool 
   }
 }
 
+// Rows adjacent in memory, vector form (RF_VEC on an RL_COLS request: the row
+// count times the element size is a multiple of 16 bytes and the base is
+// 16-byte aligned): lane l of row group gi owns the GE adjacent rows
+// gi * 32 GE + GE l .. + GE - 1 and reads them as one 16-byte load per
+// column, kRedVU columns in flight; q.rg = 32 GE rows per group.
+__device__ __forceinline__ void red_cols_vec(const Exec& ex, const ReqView& q, bool mean,
+                                             uint32_t k) {
+  const int lane = ex.lane;
+  const int64_t C = q.inner, R = q.numel;
+  const int GE = q.dta == kF32 ? 4 : 8;
+  const int es = q.dta == kF32 ? 4 : 2;
+  const uint32_t nseg = q.nseg;
+  const int64_t gi = k / nseg;
+  const uint32_t seg = k % nseg;
+  const int64_t r0 = gi * q.rg + (int64_t)GE * lane;
+  const bool valid = r0 < R;  // R is a multiple of GE, so the whole group is in range
+  const int64_t c0 = (int64_t)seg * q.chunk;
+  const int64_t c1 = min(C, c0 + (int64_t)q.chunk);
+  const int64_t sc = q.sa_in;
+  const uint8_t* p = reinterpret_cast<const uint8_t*>(q.a);
+  float acc[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+  if (valid) {
+#pragma unroll 1
+    for (int64_t c = c0; c < c1; c += kRedVU) {
+      uint4 w[kRedVU];
+#pragma unroll
+      for (int u = 0; u < kRedVU; ++u) {
+        w[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (c + u < c1) w[u] = *reinterpret_cast<const uint4*>(p + (r0 + (c + u) * sc) * es);
+      }
+#pragma unroll
+      for (int u = 0; u < kRedVU; ++u) {
+        if (c + u < c1) {
+          if (q.dta == kF32) {
+            acc[0] += __uint_as_float(w[u].x);
+            acc[1] += __uint_as_float(w[u].y);
+            acc[2] += __uint_as_float(w[u].z);
+            acc[3] += __uint_as_float(w[u].w);
+          } else {
+            float v[8];
+            if (q.dta == kF16) {
+              const uint32_t uu[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&uu[t]));
+                v[2 * t] = f.x;
+                v[2 * t + 1] = f.y;
+              }
+            } else {
+              bf2_to_f(w[u].x, v[0], v[1]);
+              bf2_to_f(w[u].y, v[2], v[3]);
+              bf2_to_f(w[u].z, v[4], v[5]);
+              bf2_to_f(w[u].w, v[6], v[7]);
+            }
+#pragma unroll
+            for (int t = 0; t < 8; ++t) acc[t] += v[t];
+          }
+        }
+      }
+    }
+  }
+  if (nseg == 1) {
+    if (valid)
+      for (int t = 0; t < GE; ++t) st1(q.o, q.dto, (r0 + t) * q.so_row, red_finish(acc[t], mean, C));
+    return;
+  }
+  // partial sums of this segment: part[(gi * nseg + seg) * rg + row in group]
+  float* part = ex.scratch + q.part + ((int64_t)gi * nseg) * q.rg;
+  if (valid)
+    for (int t = 0; t < GE; ++t) part[(int64_t)seg * q.rg + GE * lane + t] = acc[t];
+  uint32_t* cnt = ex.counters + q.cnt + gi;
+  if (combine_arrive(ex, cnt, nseg)) {
+    if (valid) {
+      for (int t = 0; t < GE; ++t) {
+        float s = 0.f;
+        for (uint32_t i = 0; i < nseg; ++i) s += __ldcg(part + (int64_t)i * q.rg + GE * lane + t);
+        st1(q.o, q.dto, (r0 + t) * q.so_row, red_finish(s, mean, C));
+      }
+    }
+    if (lane == 0) *cnt = 0u;
+  }
+}
+
 // Anything else: one lane per output element, serial over the reduced
 // elements with the first reduced axis varying fastest (the order of the
 // reference's generic path, pytorch_ext/gpuos_ext.cpp:794-798).
@@ -827,6 +946,56 @@ __device__ __forceinline__ void red_generic(const Exec& ex, const ReqView& q, co
       acc += ld1(q.a, q.dta, ib + off);
     }
     st1(q.o, q.dto, ob, red_finish(acc, mean, q.inner));
+  }
+}
+
+// Anything else with at least 64 reduced elements per output (q.rg == 1): a
+// segmented reduction, one warp per output: the lanes split the reduced
+// index space, with the last reduced axis (normally the one of smallest
+// stride) varying fastest so that neighbouring lanes read neighbouring
+// elements; four raw loads in flight per lane, then a shuffle tree.
+__device__ __forceinline__ void red_generic_warp(const Exec& ex, const ReqView& q, const ExtRec* x,
+                                                 bool mean, uint32_t k) {
+  const int lane = ex.lane;
+  const int64_t o0 = (int64_t)k * q.chunk;
+  const int64_t o1 = min(q.numel, o0 + (int64_t)q.chunk);
+  const int nd = x->ndim, rd = x->rdim;
+  const int64_t inner = q.inner;
+  constexpr int U = 4;
+  for (int64_t oi = o0; oi < o1; ++oi) {
+    int64_t rem = oi, ib = 0, ob = 0;
+    for (int d = nd - 1; d >= 0; --d) {
+      const int64_t sz = x->sizes[d];
+      const int64_t i = rem % sz;
+      rem /= sz;
+      ib += i * x->sa[d];
+      ob += i * x->so[d];
+    }
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 1
+    for (int64_t rv = lane; rv < inner; rv += 32 * U) {
+      uint32_t w[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        w[u] = 0u;
+        const int64_t r = rv + 32 * u;
+        if (r < inner) {
+          int64_t t = r, off = 0;
+          for (int j = rd - 1; j >= 0; --j) {
+            const int64_t sz = x->rsizes[j];
+            off += (t % sz) * x->rstrides[j];
+            t /= sz;
+          }
+          w[u] = ld1_raw(q.a, q.dta, ib + off);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (rv + 32 * u < inner) (u & 1 ? acc1 : acc0) += cvt1(w[u], q.dta);
+    }
+    float acc = acc0 + acc1;
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(GPUOS_FULL, acc, off);
+    if (lane == 0) st1(q.o, q.dto, ob, red_finish(acc, mean, inner));
   }
 }
 
@@ -861,7 +1030,11 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
   }
   const bool mean = (v == V_MEAN);
   if (q.layout == RL_ROWS) red_rows(ex, q, mean, k);
-  else if (q.layout == RL_COLS) red_cols(ex, q, mean, k);
+  else if (q.layout == RL_COLS) {
+    if (q.flags & RF_VEC) red_cols_vec(ex, q, mean, k);
+    else red_cols(ex, q, mean, k);
+  }
+  else if (q.rg == 1) red_generic_warp(ex, q, x, mean, k);
   else red_generic(ex, q, x, mean, k);
 #endif
 }
@@ -898,7 +1071,8 @@ __device__ __forceinline__ void finish_batch(const Exec& ex) {
 __device__ __forceinline__ Exec bind_batch(const uint8_t* payload, const BatchHdr& h,
                                            BatchState* st, volatile uint64_t* done_ring,
                                            uint64_t* done_dev, uint64_t wait_limit_ns,
-                                           volatile uint64_t* dur_ring = nullptr) {
+                                           volatile uint64_t* dur_ring = nullptr,
+                                           const Tables* tab = nullptr) {
   Exec ex;
   ex.base = payload;
   ex.st = st;
@@ -917,6 +1091,7 @@ __device__ __forceinline__ Exec bind_batch(const uint8_t* payload, const BatchHd
   ex.done_ring = done_ring;
   ex.done_dev = done_dev;
   ex.dur_ring = dur_ring;
+  ex.tab = tab;
   ex.wait_limit_ns = wait_limit_ns;
   ex.lane = threadIdx.x & 31;
   return ex;

@@ -246,7 +246,7 @@ struct alignas(64) DevCtrl {
 // copy, no granule table.  Warp g of W runs the chunks
 // [g * nchunk / W, (g + 1) * nchunk / W), so the warps of one SM work on
 // neighbouring chunks, which the host has grouped by operator.
-static constexpr int kLeanThreads = 1024;   // one CTA per SM
+static constexpr int kLeanThreads = 512;    // one CTA per SM, room for the next batch's
 static constexpr int kLeanPar = 16;         // distinct (p0, p1) pairs per batch
 static constexpr int kLeanMaxReq = 512;     // largest parameter block (about 22 KB)
 
@@ -294,6 +294,7 @@ struct WorkerArgs {
   volatile uint64_t* done_ring;
   volatile uint64_t* retired_ring;
   volatile uint64_t* dur_ring;   // device time of each batch (first CTA in -> last chunk), ns
+  const Tables* tab;             // device copy of the jump table (slot requests resolve here)
   uint64_t start_seq;
   uint64_t wait_limit_ns;        // bound of every wait inside a batch
   uint64_t idle_ns;              // ingest: stop after this long without a batch

@@ -14,12 +14,17 @@ gpuos_jit_batch_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* s
                        volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
   __shared__ ExtRec ext[kWarpsPerCta];
   __shared__ uint32_t cta_chunks;
-  if (threadIdx.x == 0) cta_chunks = 0;
+  __shared__ StageSync ss;
+  if (threadIdx.x == 0) {
+    cta_chunks = 0;
+    ss.seen = 0;
+    ss.poller = 0;
+  }
   __syncthreads();
   const Exec ex = bind_batch(payload, hdr, st, done_ring, nullptr, wait_limit_ns);
   const int warp = threadIdx.x >> 5;
   const uint32_t count = warp_batch(ex, blockIdx.x * kWarpsPerCta + warp,
-                                    gridDim.x * kWarpsPerCta, &ext[warp]);
+                                    gridDim.x * kWarpsPerCta, &ext[warp], &ss);
   // without stage barriers nothing waits on the batch's counters: the kernel's
   // completion completes the batch, and its warps leave as soon as they are done
   if (posts_own_errors(ex)) return;

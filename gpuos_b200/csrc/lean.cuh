@@ -8,7 +8,8 @@
 // per thread, so an SM holds 16 warps, and neighbouring warps run different
 // operator bodies out of one large kernel: a third of the stall cycles were
 // instruction fetch.  Here:
-//   * one CTA of 1024 threads per SM, 64 registers per thread (32 warps);
+//   * one CTA of 512 threads per SM at 64 registers per thread (16 warps):
+//     half the SM's registers, so the next batch's CTA fits beside it;
 //   * warp g of W runs the contiguous chunk range [g n / W, (g + 1) n / W):
 //     the host sorts a batch's requests by operator, so the warps of an SM
 //     run one or two operator bodies;
@@ -36,11 +37,11 @@ __device__ __forceinline__ void gdc_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// 4-element groups per lane in flight per round: 4 for the light operators,
-// 2 for those with a division, a square root or a transcendental function.
-template <int V>
+// 4-element groups per lane in flight per round: GL for the light operators,
+// GL / 2 for those with a division, a square root or a transcendental function.
+template <int V, int GL>
 __device__ __forceinline__ constexpr int lean_groups() {
-  return op_unroll<V>() == 2 ? 4 : 2;
+  return op_unroll<V>() == 2 ? GL : GL / 2;
 }
 
 struct LeanCur {
@@ -52,10 +53,10 @@ struct LeanCur {
 };
 
 // elements [e0, e0 + n) of one request, n > 0 (unary operators ignore b)
-template <int V, int N>
+template <int V, int N, int GL>
 __device__ __forceinline__ void lean_chunk(const LeanCur& u, const LeanBatch<N>& bt, uint32_t e0,
                                            uint32_t n, int lane) {
-  constexpr int kG = lean_groups<V>();
+  constexpr int kG = lean_groups<V, GL>();
   constexpr bool kBin = V == V_ADD || V == V_MUL || V == V_SUB || V == V_DIV0 || V == V_DIV ||
                         V == V_MAX || V == V_MIN || V == V_POW;
   const float p0 = bt.h.par[u.pidx][0], p1 = bt.h.par[u.pidx][1];
@@ -93,9 +94,9 @@ __device__ __forceinline__ void lean_chunk(const LeanCur& u, const LeanBatch<N>&
   }
 }
 
-#define GPUOS_LEAN_CASE(V) case V: lean_chunk<V>(u, bt, e0, n, lane); return;
+#define GPUOS_LEAN_CASE(V) case V: lean_chunk<V, N, GL>(u, bt, e0, n, lane); return;
 
-template <int N>
+template <int N, int GL>
 __device__ __forceinline__ void lean_dispatch(const LeanCur& u, const LeanBatch<N>& bt, uint32_t e0,
                                               uint32_t n, int lane) {
   switch (u.op) {
@@ -116,7 +117,7 @@ __device__ __forceinline__ void lean_decode(LeanCur& u, const LeanBatch<N>& bt, 
   u.pidx = q.pidx;
 }
 
-template <int N>
+template <int N, int THREADS, int GL>
 __device__ __forceinline__ void lean_batch(const LeanBatch<N>& bt) {
   __shared__ uint32_t s_cb[N + 1];
   const LeanHdr& h = bt.h;
@@ -129,7 +130,7 @@ __device__ __forceinline__ void lean_batch(const LeanBatch<N>& bt) {
   for (uint32_t i = threadIdx.x; i <= nreq; i += blockDim.x) s_cb[i] = bt.cb[i];
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  constexpr uint32_t kWarps = kLeanThreads / 32;
+  constexpr uint32_t kWarps = THREADS / 32;
   const uint64_t W = (uint64_t)gridDim.x * kWarps;
   const uint64_t gw = (uint64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
   const uint32_t nchunk = h.nchunk;
@@ -160,7 +161,7 @@ __device__ __forceinline__ void lean_batch(const LeanBatch<N>& bt) {
     }
     const uint32_t e0 = (c - rbase) * u.chunk;
     const uint32_t n = min(u.chunk, u.numel - e0);
-    lean_dispatch(u, bt, e0, n, lane);
+    lean_dispatch<N, GL>(u, bt, e0, n, lane);
   }
   // completion: every CTA releases its stores, the last one posts the word
   __syncthreads();

@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <thread>
 
 #if defined(__x86_64__)
@@ -374,6 +375,7 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   total_warps_ = ctas * gpuos_cta_threads() / 32;
   lean_grid_ = sm_count_;
   lean_on_ = env_double("GPUOS_LEAN", 1.0) != 0.0;
+  lean_warps_ = sm_count_ * kLeanThreads / 32;
   lean_buf_.resize(gpuos_lean_params_size(2));
 
   GCU(cudaStreamCreateWithFlags(&s_worker_, cudaStreamNonBlocking));
@@ -424,7 +426,11 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   }
   tab_.slot[0] = SlotEntry{V_ADD, 0.f, 0.f, 2};
   tab_.slot[1] = SlotEntry{V_MUL, 0.f, 0.f, 2};
-  GCU(cudaDeviceSynchronize());
+  GCU(cudaMalloc(reinterpret_cast<void**>(&dtab_), sizeof(Tables)));
+  GCU(cudaMemcpy(dtab_, &tab_, sizeof(Tables), cudaMemcpyHostToDevice));
+  // the memsets above ran on the legacy stream; a device-wide synchronisation
+  // would also wait for another executor's persistent worker on this device
+  GCU(cudaStreamSynchronize(nullptr));
   started_ = true;
   if (opt_.mode == GPUOS_MODE_PERSISTENT) launch_worker_locked(0);
 }
@@ -443,8 +449,10 @@ void Executor::ensure_scratch_locked() {
   counters_cap_ = 4ull << 20;   // u32
   GCU(cudaMalloc(reinterpret_cast<void**>(&partials_), partials_cap_ * sizeof(float)));
   GCU(cudaMalloc(reinterpret_cast<void**>(&counters_), counters_cap_ * sizeof(uint32_t)));
-  GCU(cudaMemset(counters_, 0, counters_cap_ * sizeof(uint32_t)));
-  GCU(cudaDeviceSynchronize());
+  // on the executor's own stream: a device-wide synchronisation would wait
+  // for the persistent worker
+  GCU(cudaMemsetAsync(counters_, 0, counters_cap_ * sizeof(uint32_t), s_ctrl_));
+  GCU(cudaStreamSynchronize(s_ctrl_));
   part_alloc_.init(partials_cap_);
   cnt_alloc_.init(counters_cap_);
 }
@@ -666,6 +674,29 @@ void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
         p.partials = (uint64_t)R * q.nseg;
         p.counters = (uint64_t)R;
       }
+    } else if (sr == 1 && mk <= 1 && mr == 1 && (q.a & 15) == 0 && ((sc * e) & 15) == 0 &&
+               R % (16 / e) == 0 && R >= 16 * (16 / e)) {
+      // rows adjacent, 16-byte aligned: each lane reads 16 bytes of adjacent
+      // rows per column (red_cols_vec); chunks of 32 x GE rows by `chunk` columns
+      q.layout = RL_COLS;
+      q.flags |= RF_VEC;
+      const int64_t GE = 16 / e;
+      const uint32_t rg = (uint32_t)(32 * GE);
+      int64_t seglen = std::max<int64_t>(8, 16384 / rg);
+      int64_t nseg = std::max<int64_t>(1, (C + seglen - 1) / seglen);
+      if (nseg > 256) {
+        seglen = (C + 255) / 256;
+        nseg = (C + seglen - 1) / seglen;
+      }
+      const int64_t ngroups = (R + rg - 1) / rg;
+      q.rg = rg;
+      q.chunk = (uint32_t)seglen;
+      q.nseg = (uint32_t)nseg;
+      p.nchunk = (uint32_t)(ngroups * nseg);
+      if (nseg > 1) {
+        p.partials = (uint64_t)(ngroups * nseg * rg);
+        p.counters = (uint64_t)ngroups;
+      }
     } else {
       q.layout = RL_COLS;
       const uint32_t rg = std::min<uint32_t>(32, pow2_ceil((uint64_t)std::max<int64_t>(R, 1)));
@@ -688,8 +719,15 @@ void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
     }
   } else {
     q.layout = RL_GENERIC;
-    q.chunk = 32;
-    p.nchunk = (uint32_t)((R + 31) / 32);
+    if (C >= 64) {
+      // a warp per output (red_generic_warp), a few outputs per chunk
+      q.rg = 1;
+      q.chunk = (uint32_t)std::max<int64_t>(1, kSeg / C);
+    } else {
+      // a lane per output (red_generic), 32 outputs per chunk
+      q.chunk = 32;
+    }
+    p.nchunk = (uint32_t)((R + q.chunk - 1) / q.chunk);
     p.has_ext = true;
     std::memset(&p.ext, 0, sizeof(p.ext));
     p.ext.ndim = mk;
@@ -998,7 +1036,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     GCU(cudaStreamIsCapturing(stream, &cap));
     lean = cap == cudaStreamCaptureStatusNone;
   }
-  const uint64_t warps = lean ? (uint64_t)lean_grid_ * (kLeanThreads / 32)
+  const uint64_t warps = lean ? (uint64_t)std::max(1, lean_warps_)
                               : (uint64_t)std::max(1, total_warps_);
   uint64_t ce = align_up(std::max<uint64_t>(1, ew_work / (2 * warps)), 512);
   ce = std::min<uint64_t>(std::max<uint64_t>(ce, 512), 8192);
@@ -1125,12 +1163,16 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   uint32_t* cbp = reinterpret_cast<uint32_t*>(base + cb_off);
   ExtRec* ext = reinterpret_cast<ExtRec*>(base + ext_off);
   uint64_t pf = 0, pc = coff, xi = 0;
+  const bool jit_batch = var[0] >= V_JIT_BASE;  // a batch is all custom or all precompiled
+  // the persistent worker resolves slot requests itself, from its copy of the
+  // jump table, when it starts them
+  const bool dev_resolve = opt_.mode == GPUOS_MODE_PERSISTENT && !jit_batch;
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + order[r]];
     Req q = p.r;
-    // the operator (and parameters) the request's slot names now: the
-    // device runs the record as it stands
-    if (q.flags & RF_SLOT) {
+    // otherwise the operator (and parameters) the request's slot names now:
+    // the device runs the record as it stands
+    if ((q.flags & RF_SLOT) && !dev_resolve) {
       const int s = q.op;
       const int phys = (s >= 0 && s < kMaxSlots) ? tab_.alias[s] : -1;
       if (phys >= 0 && phys < kMaxSlots) {
@@ -1139,7 +1181,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       }
       q.flags = (uint8_t)(q.flags & ~RF_SLOT);
     }
-    q.op = var[order[r]] < 0 ? kOpNone : (uint16_t)var[order[r]];
+    if (!(q.flags & RF_SLOT)) q.op = var[order[r]] < 0 ? kOpNone : (uint16_t)var[order[r]];
     if (p.has_ext) {
       ext[xi] = p.ext;
       q.ext = (uint32_t)(ext_off + sizeof(ExtRec) * xi);
@@ -1181,7 +1223,6 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
         if (stage_first[order[r]] == last) w[r] = cb[last] + 1u;
     }
   }
-  const bool jit_batch = var[0] >= V_JIT_BASE;  // a batch is all custom or all precompiled
   if (jit_batch && opt_.mode == GPUOS_MODE_PERSISTENT) {
     // Custom expressions do not run in the resident worker: the batch runs
     // after every earlier batch, on its own launch, before any later one.  It
@@ -1400,7 +1441,9 @@ bool Executor::publish_lean(std::unique_lock<std::mutex>& lk, std::vector<Pendin
     GCU(cudaEventRecord(last_event_, last_stream_));
     GCU(cudaStreamWaitEvent(stream, last_event_, 0));
   }
-  const int grid = (int)std::min<uint64_t>((uint64_t)lean_grid_, std::max<uint64_t>(1, nchunk / 32));
+  const int wpc = kLeanThreads / 32;
+  const int grid = (int)std::min<uint64_t>((uint64_t)lean_grid_,
+                                           std::max<uint64_t>(1, (nchunk + wpc - 1) / wpc));
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   if (timing_) {
     for (cudaEvent_t* e : {&e0, &e1}) {
@@ -1626,6 +1669,7 @@ void Executor::launch_worker_locked(uint64_t start) {
       hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(retired_ring_) - hostblk_));
   w.dur_ring = reinterpret_cast<volatile uint64_t*>(
       hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(dur_ring_) - hostblk_));
+  w.tab = dtab_;
   w.start_seq = start;
   w.wait_limit_ns = wait_limit_ns_;
   w.idle_ns = idle_ns_;
@@ -1690,6 +1734,7 @@ int Executor::register_elementwise(const std::string& key, const std::string& ex
   }
   const int slot = next_slot_++;
   tab_.slot[slot] = SlotEntry{v, p0, p1, arity};
+  push_tables_locked();
   slot_of_key_.emplace(key, slot);
   return slot;
 }
@@ -1705,6 +1750,7 @@ int Executor::register_reduce(const std::string& key, const std::string& op_name
   if (next_slot_ >= kMaxSlots) throw GError(GPUOS_EINVAL, "jump table is full (128 slots)");
   const int slot = next_slot_++;
   tab_.slot[slot] = SlotEntry{v, 0.f, 0.f, 1};
+  push_tables_locked();
   slot_of_key_.emplace(key, slot);
   return slot;
 }
@@ -1714,6 +1760,17 @@ void Executor::set_alias(int logical, int physical) {
     throw GError(GPUOS_EINVAL, "slot out of range");
   std::lock_guard<std::mutex> lk(mu_);
   tab_.alias[logical] = physical;
+  push_tables_locked();
+}
+
+// Publish the jump table to its device copy (the persistent worker reads it
+// with acquire loads when it starts a slot request); returns once the copy
+// has landed, so a swap is visible to every request the worker starts after
+// the call returns.
+void Executor::push_tables_locked() {
+  DeviceGuard g(device_);
+  GCU(cudaMemcpyAsync(dtab_, &tab_, sizeof(Tables), cudaMemcpyHostToDevice, s_ctrl_));
+  GCU(cudaStreamSynchronize(s_ctrl_));
 }
 
 void Executor::set_slot(int slot, int variant, float p0, float p1) {
@@ -1727,6 +1784,7 @@ void Executor::set_slot(int slot, int variant, float p0, float p1) {
                      variant == V_DIV0 || variant == V_DIV || variant == V_MAX ||
                      variant == V_MIN || variant == V_POW) ? 2 : 1;
   tab_.slot[slot] = SlotEntry{variant, p0, p1, arity};
+  push_tables_locked();
 }
 
 void Executor::get_slot(int slot, int* variant, float* p0, float* p1, int* alias) {
@@ -1823,12 +1881,28 @@ void Executor::shutdown() {
     hctrl_->quit = 1u;
     std::atomic_thread_fence(std::memory_order_seq_cst);
     const auto t0 = std::chrono::steady_clock::now();
+    bool stopped = true;
     while (cudaStreamQuery(s_worker_) == cudaErrorNotReady) {
       const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-      if (el > sync_timeout_s_ + idle_ns_ * 1e-9) break;
+      if (el > sync_timeout_s_ + idle_ns_ * 1e-9) {
+        stopped = false;
+        break;
+      }
       std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
     worker_launched_ = false;
+    if (!stopped) {
+      // Freeing device memory synchronises the device, which would wait for
+      // the worker without bound: leave the executor's memory to process exit.
+      throw GError(GPUOS_ETIMEOUT,
+                   "the persistent worker did not stop (exit reason " +
+                       std::to_string(hctrl_->exit_reason) + ", worker errors " +
+                       std::to_string(hctrl_->err) + ", staged " +
+                       std::to_string(hctrl_->staged) + ", processed " +
+                       std::to_string(hctrl_->processed) + ", published " +
+                       std::to_string(next_seq_) + "); its memory is left allocated" +
+                       (first_error.empty() ? std::string() : "; " + first_error));
+    }
   }
   cudaStreamSynchronize(s_own_);
   cudaStreamSynchronize(s_ctrl_);
@@ -1842,6 +1916,7 @@ void Executor::shutdown() {
   jit_word_ = nullptr;
   if (ring_) cudaFree(ring_);
   if (dctrl_) cudaFree(dctrl_);
+  if (dtab_) cudaFree(dtab_);
   for (cudaEvent_t& e : done_ev_)
     if (e) cudaEventDestroy(e);
   for (cudaEvent_t& e : copy_ev_)
@@ -1863,7 +1938,7 @@ void Executor::shutdown() {
   if (s_own_) cudaStreamDestroy(s_own_);
   if (s_copy_) cudaStreamDestroy(s_copy_);
   s_copy_ = nullptr;
-  states_ = nullptr; ring_ = nullptr; dctrl_ = nullptr; partials_ = nullptr; counters_ = nullptr;
+  states_ = nullptr; ring_ = nullptr; dctrl_ = nullptr; dtab_ = nullptr; partials_ = nullptr; counters_ = nullptr;
   arena_ = nullptr; hostblk_ = nullptr; last_event_ = nullptr;
   s_worker_ = s_ctrl_ = s_own_ = nullptr;
   if (!first_error.empty()) throw GError(GPUOS_EDEVICE, "shutdown: " + first_error);
@@ -1912,22 +1987,63 @@ int32_t gpuos_abi_version(void) { return GPUOS_ABI_VERSION; }
 
 const char* gpuos_last_error(void) { return gpuos::t_last_error.c_str(); }
 
+// The executor most recently created on each device (the reference-named
+// hot-swap shims act on it).
+namespace {
+std::mutex g_cur_mu;
+Executor* g_cur[64] = {nullptr};
+}  // namespace
+
 int32_t gpuos_executor_create(int32_t device, const gpuos_options* opt, gpuos_executor** out) {
   return guard([&] {
     if (!out) throw GError(GPUOS_EINVAL, "out is NULL");
     gpuos_options o;
     std::memset(&o, 0, sizeof(o));
     if (opt) o = *opt;
-    *out = reinterpret_cast<gpuos_executor*>(new Executor(device, o));
+    Executor* e = new Executor(device, o);
+    *out = reinterpret_cast<gpuos_executor*>(e);
+    std::lock_guard<std::mutex> lk(g_cur_mu);
+    if (device >= 0 && device < 64) g_cur[device] = e;
   });
 }
 
 int32_t gpuos_executor_destroy(gpuos_executor* ex) {
   return guard([&] {
     Executor* e = X(ex);
+    {
+      std::lock_guard<std::mutex> lk(g_cur_mu);
+      for (Executor*& c : g_cur)
+        if (c == e) c = nullptr;
+    }
     std::unique_ptr<Executor> hold(e);
     e->shutdown();
   });
+}
+
+// cudaSuccess / cudaErrorInvalidValue, as the reference's shims return
+static int32_t shim(const std::function<void(Executor*)>& f) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    gpuos::set_last_error("no current CUDA device");
+    return 1;
+  }
+  std::lock_guard<std::mutex> lk(g_cur_mu);
+  if (!g_cur[dev]) {
+    gpuos::set_last_error("no executor was created on the current device");
+    return 1;
+  }
+  const int32_t rc = guard([&] { f(g_cur[dev]); });
+  return rc == GPUOS_OK ? 0 : 1;
+}
+
+int32_t gpu_set_op_table_async(int32_t index, uint64_t fn, void* stream) {
+  (void)stream;
+  return shim([&](Executor* e) { e->set_slot(index, (int)(int64_t)fn, 0.f, 0.f); });
+}
+
+int32_t gpu_set_alias_async(int32_t logical_id, int32_t physical_slot, void* stream) {
+  (void)stream;
+  return shim([&](Executor* e) { e->set_alias(logical_id, physical_slot); });
 }
 
 int32_t gpuos_submit_builtin(gpuos_executor* ex, int32_t op, const gpuos_tensor* a,

@@ -212,6 +212,8 @@ class Executor {
   std::string cuda_err_;        // first CUDA error a completion query reported
 
   Tables tab_;
+  Tables* dtab_ = nullptr;   // device copy, read by the persistent worker (slot requests)
+  void push_tables_locked();
   std::unordered_map<std::string, int> slot_of_key_;
   // custom expressions (variants V_JIT_BASE + k) and the batch kernel linked with them
   std::vector<std::string> jit_exprs_;
@@ -237,6 +239,7 @@ class Executor {
   // with programmatic dependent launch, completed by a word in done_ring_
   bool lean_on_ = true;
   int lean_grid_ = 0;                 // CTAs of the lean kernel (one per SM)
+  int lean_warps_ = 0;                // warps of a full lean grid
   std::vector<uint8_t> lean_seq_ = std::vector<uint8_t>(kDoneRing, 0);  // batch seq is lean
   std::vector<uint8_t> lean_buf_;     // parameter block being built (largest size class)
   bool lean_prev_in_flush_ = false;   // the last op this flush put on the stream is a lean batch

@@ -170,8 +170,24 @@ int32_t gpuos_set_alias(gpuos_executor* ex, int32_t logical, int32_t physical);
 
 /* Online hot swap: overwrite what a physical slot runs (replaces
  * gpu_set_op_table_async, persistent_kernel.cu:220-222; takes an operator
- * id instead of a raw device function pointer). */
+ * id instead of a raw device function pointer).  In persistent mode the
+ * worker resolves a slot request from its device copy of the table when it
+ * starts the request, so a swap reaches batches already published but not yet
+ * started, as in the reference; in stream mode a request's slot is resolved
+ * when it is flushed. */
 int32_t gpuos_set_slot(gpuos_executor* ex, int32_t slot, int32_t variant, float p0, float p1);
+
+/* The reference's hot-swap entry points under their own names, for programs
+ * ported from its tests (gpu_set_op_table_async / gpu_set_alias_async,
+ * src/persistent_kernel.cu:220-226).  They act on the executor most recently
+ * created on the calling thread's current device.  `fn` is an operator id
+ * (gpuos_variant_by_name, or the operator a registered slot holds, from
+ * gpuos_get_slot) where the reference takes a device function pointer, as
+ * gpuos_set_slot does.  The table is published before the call returns, so
+ * `stream` is not used.  Return 0 (cudaSuccess), or 1 (cudaErrorInvalidValue)
+ * with the message in gpuos_last_error(). */
+int32_t gpu_set_op_table_async(int32_t index, uint64_t fn, void* stream);
+int32_t gpu_set_alias_async(int32_t logical_id, int32_t physical_slot, void* stream);
 
 /* Read a slot (variant id, parameters) and the alias of a logical slot. */
 int32_t gpuos_get_slot(gpuos_executor* ex, int32_t slot, int32_t* variant, float* p0, float* p1,

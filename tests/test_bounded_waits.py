@@ -70,3 +70,23 @@ def test_host_wait_times_out_then_completes():
         assert e.value.code == ETIMEOUT
         ex.wait(ticket, 30.0)
         assert torch.equal(o, a + b)
+
+
+@pytest.mark.parametrize("mode", [C.MODE_PERSISTENT, C.MODE_STREAM], ids=["persistent", "stream"])
+def test_device_time_is_accounted(mode):
+    """stats.dev_ns grows by the device time of completed batches (first CTA
+    in -> last chunk) for the persistent worker and lean stream batches."""
+    with C.Executor(0, mode=mode) as ex:
+        a = torch.randn(1 << 20, device=DEV)
+        b = torch.randn(1 << 20, device=DEV)
+        o = torch.empty_like(a)
+        before = ex.stats()["dev_ns"]
+        for _ in range(4):
+            ex.builtin(C.OP_ADD, a, b, o)
+            ex.flush(sync=True)
+        after = ex.stats()
+        assert torch.equal(o, a + b)
+        d = after["dev_ns"] - before
+        assert 0 < d < 4 * 50_000_000, d   # a 12 MB batch: microseconds, not 50 ms
+        if mode == C.MODE_STREAM:
+            assert after["lean"] >= 4

@@ -24,7 +24,7 @@ HEADER = (ROOT / "include" / "gpuos_b200.h").read_text()
 
 
 def declared():
-    return sorted(set(re.findall(r"^\s*(?:int32_t|const char\*)\s+(gpuos_\w+)\(", HEADER, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int32_t|const char\*)\s+(gpu(?:os)?_\w+)\(", HEADER, re.M)))
 
 
 def test_header_symbols_exported():
@@ -132,7 +132,16 @@ def test_plan_reductions():
     assert p["rg"] == 4 and p["chunk"] % 8 == 0
     xt = torch.randn(3000, 100).t()
     p = C.plan_reduce(C.variant("mean"), xt, torch.empty(100), [1], False)
-    assert (p["layout"], p["sa_row"], p["sa_in"], p["rg"]) == (1, 1, 100, 32)
+    # rows adjacent and 16-byte aligned: lanes read 16 bytes of 4 rows (128 per group)
+    assert (p["layout"], p["sa_row"], p["sa_in"], p["rg"]) == (1, 1, 100, 128)
+    assert p["flags"] & 2 and p["chunk"] == 128 and p["nseg"] == 24
+    assert p["nchunk"] == 24 and p["partials"] == 24 * 128 and p["counters"] == 1
+    xb = torch.randn(3000, 256, dtype=torch.bfloat16).t()    # bf16: 8 rows per lane
+    p = C.plan_reduce(C.variant("sum"), xb, torch.empty(256, dtype=torch.bfloat16), [1], False)
+    assert p["flags"] & 2 and p["rg"] == 256 and p["chunk"] == 64
+    xo = torch.randn(3000, 99).t()                              # 99 rows: not a multiple of 4
+    p = C.plan_reduce(C.variant("mean"), xo, torch.empty(99), [1], False)
+    assert (p["layout"], p["rg"]) == (1, 32) and not p["flags"] & 2
     assert p["nseg"] > 1 and p["partials"] == 4 * p["nseg"] * 32
     w = torch.randn(8, 16, 32)
     p = C.plan_reduce(C.variant("sum"), w, torch.empty(32), [0, 1], False)
@@ -143,6 +152,11 @@ def test_plan_reductions():
     wq = torch.randn(8, 16, 32).permute(2, 0, 1)     # reduced dims 0 and 2 do not
     p = C.plan_reduce(C.variant("sum"), wq, torch.empty(8), [0, 2], False)
     assert p["layout"] == 2 and p["has_ext"] == 1 and p["inner"] == 32 * 16
+    # 512 reduced elements per output: a warp per output, 8192 / 512 outputs a chunk
+    assert p["rg"] == 1 and p["chunk"] == 16 and p["nchunk"] == 1
+    wr = torch.randn(8, 4, 6).permute(2, 0, 1)       # 24 per output: a lane per output
+    p = C.plan_reduce(C.variant("sum"), wr, torch.empty(8), [0, 2], False)
+    assert p["layout"] == 2 and p["rg"] == 0 and p["chunk"] == 32
     with pytest.raises(C.GpuosError):
         C.plan_reduce(C.variant("sum"), x, torch.empty(7), [1], False)
 

@@ -1,5 +1,6 @@
 """The multi-rank plumbing of bench.py on CPU: two gloo ranks, as torchrun
-would start them, agree on the max over ranks and the whole-job rate."""
+would start them, agree on the max over ranks, the whole-job rate and the
+per-rank step times."""
 import os
 import socket
 
@@ -23,8 +24,9 @@ def _rank(rank, world, port, q):
         t = 1.0 + rank  # rank 1 is the slower one
         m = bench.allmax(t, world)
         rate = bench.whole_job_rate(16384, t, world)
+        per_rank = bench.allgather(t, world)
         bench.barrier(world)
-        q.put((rank, m, rate))
+        q.put((rank, m, rate, per_rank))
     finally:
         dist.destroy_process_group()
 
@@ -40,6 +42,7 @@ def test_two_ranks_max_and_rate():
         p.join(timeout=120)
         assert p.exitcode == 0
     got = sorted(q.get(timeout=10) for _ in range(2))
-    for rank, m, rate in got:
+    for rank, m, rate, per_rank in got:
         assert m == 2.0
         assert rate == pytest.approx(2 * 16384 / 2.0)
+        assert per_rank == [1.0, 2.0]

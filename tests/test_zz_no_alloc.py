@@ -1,10 +1,13 @@
 """gpuos_reduce_rows_noalloc: the row reduction that allocates nothing.
 
 Its results are checked against the executor's own reduction entry point
-(gpuos_submit_reduce + gpuos_flush) on the same inputs, within the reduction
-tolerance of the parity tests (|got - want| <= 1e-5 * sum|x| per row), on two
-calls in a row: the second call reuses the static scratch the first one left
-behind.  The file is named to run last, and passes alone in a fresh process.
+(gpuos_submit_reduce + gpuos_flush) and against the double-precision sum of
+the same inputs, within the reduction tolerance of the parity tests
+(|got - want| <= 1e-5 * sum|x| per row, plus one output ulp for 16-bit
+outputs), on two calls in a row: the second call reuses the static scratch
+the first one left behind.  A warmed call must leave the device's free memory
+unchanged.  The file is named to run last, and passes alone in a fresh
+process.
 """
 import ctypes
 
@@ -38,13 +41,19 @@ def executor_reduce(variant, x, out_dtype):
     return out
 
 
+def exact(variant, x):
+    """The double-precision sum (or mean) of every row, on the CPU."""
+    d = x.double().cpu()
+    return d.sum(dim=1) if variant == SUM else d.mean(dim=1)
+
+
 def assert_close(got, want, x):
-    mag = x.float().abs().sum(dim=1)
+    tol = RED_REL * x.float().abs().sum(dim=1).double().cpu()
     if got.dtype != torch.float32:
-        # one rounding of the fp32 result to the output type on top
-        mag = mag + want.float().abs() * (2.0 ** -7)
-    err = (got.float() - want.float()).abs()
-    assert bool((err <= RED_REL * mag + 1e-30).all()), float((err - RED_REL * mag).max())
+        # one rounding of the fp32 result to the 16-bit output type on top
+        tol = tol + want.double().abs().cpu() * 2.0 ** -7
+    err = (got.double().cpu() - want.double().cpu()).abs()
+    assert bool((err <= tol + 1e-30).all()), float((err - tol).max())
 
 
 @pytest.mark.gpu
@@ -64,11 +73,34 @@ def test_noalloc_matches_executor_on_two_calls():
     w2 = executor_reduce(MEAN, x2, torch.float32)
     assert_close(o1, w1, x1)
     assert_close(o2, w2, x2)
+    assert_close(o1.cpu(), exact(SUM, x1), x1.cpu())
+    assert_close(o2.cpu(), exact(MEAN, x2), x2.cpu())
     # and once more on the first input, now after call 2's scratch contents
     o3 = torch.empty(300, dtype=torch.float32, device=DEV)
     noalloc(SUM, x1, o3)
     torch.cuda.synchronize()
     assert_close(o3, w1, x1)
+    assert_close(o3.cpu(), exact(SUM, x1), x1.cpu())
+
+
+@pytest.mark.gpu
+def test_noalloc_allocates_nothing_and_handles_unaligned_bf16():
+    """A warmed call leaves the device's free memory as it was; a bf16 input
+    one element off 16-byte alignment with rows longer than a segment (the
+    scalar path with split rows) matches the double-precision sums."""
+    g = torch.Generator(device="cpu").manual_seed(9)
+    base = torch.randn(300 * 9001 + 1, generator=g).to(torch.bfloat16).to(DEV)
+    x = base[1:].view(300, 9001)                 # odd offset and odd row stride
+    o = torch.empty(300, dtype=torch.bfloat16, device=DEV)
+    noalloc(SUM, x, o)                            # warm: device set-up on first use
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        noalloc(SUM, x, o)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert_close(o.cpu(), exact(SUM, x), x.cpu())
+    assert_close(o, executor_reduce(SUM, x, torch.bfloat16), x)
 
 
 @pytest.mark.gpu
@@ -79,6 +111,7 @@ def test_noalloc_short_rows_and_half_output():
     noalloc(MEAN, x, o)
     torch.cuda.synchronize()
     assert_close(o, executor_reduce(MEAN, x, torch.float16), x)
+    assert_close(o.cpu(), exact(MEAN, x), x.cpu())
 
 
 def test_noalloc_rejects_sizes_beyond_the_scratch():
