@@ -4,8 +4,9 @@
 //
 //  * The host cuts each request into chunks and the batch into granules of
 //    `gran` consecutive chunks; for every granule it stores the request that
-//    owns the granule's first chunk (and that request's first chunk).  Warp g of W takes granules g, g + W, ...
-//    (no atomics), walks forward through the requests of its granules, and
+//    owns the granule's first chunk (and that request's first chunk).  Warp g
+//    of W takes the contiguous granule range [g G / W, (g + 1) G / W) (no
+//    atomics), walks forward through the requests of its granules, and
 //    decodes each request's record once.
 //  * Aligned elementwise chunks run the vector body (ew_vec: 128-bit loads,
 //    up to 8 groups of 4 elements per lane in flight); strided views and
@@ -103,8 +104,10 @@ __device__ __forceinline__ void decode(Cur& cur, const Exec& ex, const Req* rec,
   }
 }
 
+template <int BODIES>
 __device__ __forceinline__ void run_chunk(const Exec& ex, Cur& cur, uint32_t k,
                                           const ExtRec* xs) {
+  if constexpr (!(BODIES & BODY_EW)) cur.vec = false;
   if (cur.vec) {
     if (ex.flags & BF_STAGED) {
       // a scalar operand can be the output of an earlier stage: read it after
@@ -117,12 +120,13 @@ __device__ __forceinline__ void run_chunk(const Exec& ex, Cur& cur, uint32_t k,
     if (n > (int64_t)cur.u.chunk) n = cur.u.chunk;
     ew_vec_dispatch(cur.v, cur.u, cur.p0, cur.p1, e0, n, ex.lane);
   } else {
-    process_chunk(ex, load_req(cur.rec, ex.lane), cur.v, cur.p0, cur.p1, k, xs);
+    process_chunk<BODIES>(ex, load_req(cur.rec, ex.lane), cur.v, cur.p0, cur.p1, k, xs);
   }
 }
 
 // One warp's share of a batch: warp gw of W.  Returns the chunks it ran that
 // are still to be counted (all of them, unless the batch counts chunk by chunk).
+template <int BODIES = BODY_ALL>
 __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint32_t W,
                                                ExtRec* xs, StageSync* ss) {
   const int lane = ex.lane;
@@ -135,7 +139,18 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
     if (lane == 0) x = atomicAdd(&ex.st->claim, 1u);
     return __shfl_sync(GPUOS_FULL, x, 0);
   };
-  uint32_t j = staged ? claim() : gw;
+  // Without stage barriers warp gw takes the contiguous granule range
+  // [gw G / W, (gw + 1) G / W): requests are sorted by operator, so the warps
+  // of an SM run one or two operator bodies at a time.  With stage barriers
+  // granules are claimed in order.
+  uint32_t j, jend = ngran;
+  if (staged) {
+    j = claim();
+  } else {
+    j = (uint32_t)((uint64_t)gw * ngran / W);
+    jend = (uint32_t)((uint64_t)(gw + 1) * ngran / W);
+  }
+  auto next_of = [&](uint32_t x) -> uint32_t { return x + 1 < jend ? x + 1 : ngran; };
   uint32_t count = 0, waited = 0;
   int r = -1;
   uint32_t rbase = 0, rend = 0;
@@ -147,20 +162,23 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
   // static order: the entry of the granule after the next one is loaded an
   // iteration ahead, so that the next granule's record load never waits on it
   uint2 gq = make_uint2(0u, 0u);
-  if (j < ngran) {
+  if (j < jend) {
     g = __ldcg(ex.gtab + j);
-    if (!staged && j + W < ngran) gq = __ldcg(ex.gtab + j + W);
+    if (!staged) {
+      const uint32_t jq = next_of(j);
+      if (jq < ngran) gq = __ldcg(ex.gtab + jq);
+    }
     gw_rec = load_req_words(ex.recs + g.x, lane);
     g_end = __ldcg(ex.gcb + g.x + 1);
   }
-  while (j < ngran) {
-    const uint32_t jn = staged ? claim() : j + W;  // the next granule, known ahead
+  while (j < jend) {
+    const uint32_t jn = staged ? claim() : next_of(j);  // the next granule, known ahead
     uint2 gn;
     if (staged) {
       gn = jn < ngran ? __ldcg(ex.gtab + jn) : make_uint2(0u, 0u);
     } else {
       gn = gq;
-      const uint32_t jq = jn + W;
+      const uint32_t jq = jn < ngran ? next_of(jn) : ngran;
       gq = jq < ngran ? __ldcg(ex.gtab + jq) : make_uint2(0u, 0u);
     }
     uint32_t c = j * G;
@@ -221,7 +239,7 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
           __syncwarp();
         }
       }
-      run_chunk(ex, cur, c - rbase, xs);
+      run_chunk<BODIES>(ex, cur, c - rbase, xs);
       if (staged) {
         __threadfence();  // release this chunk's stores before it is counted
         __syncwarp();

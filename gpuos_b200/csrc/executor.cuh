@@ -262,22 +262,30 @@ __device__ __forceinline__ void ew_generic(const ReqView& q, const ExtRec* x, in
 
 // ---------------------------------------------------------------------------
 // 2-D elementwise tiles (EL_TILE2D): a chunk is a block of `chunk` columns of
-// every one of the request's rows.  Lane l owns columns c0 + l, c0 + l + 32,
-// ... and walks down the rows kTileU at a time, all loads of a round issued
-// raw before any is converted: the output and row-contiguous operands are
-// read and written 32 adjacent columns per instruction, and a transposed
-// operand (row stride 1) is read by each lane along its own contiguous run,
-// which L1 serves for the neighbouring rows.  No division per element; the
-// dtypes and the operator are template parameters for the combinations of
-// the broadcast configuration (-1: read at run time).
+// every one of the request's rows.  Lane l owns the kTileC columns
+// c0 + l + 32 j (j < kTileC) of each group of 32 kTileC columns and walks
+// down the rows kTileR at a time: kTileR x kTileC loads per operand in
+// flight, issued raw before any is converted.  The output and row-contiguous
+// operands move 32 adjacent columns per instruction; a transposed operand
+// (row stride 1) is read by each lane along its own contiguous runs, which L1
+// serves for the neighbouring rows.  Each column's operand pointers are set
+// up once per tile and advanced by the row strides: no division and no index
+// multiplication per element.  The dtypes and the operator are template
+// parameters for the broadcast configuration's combinations (-1: read at run
+// time).
 // ---------------------------------------------------------------------------
-static constexpr int kTileU = 8;
+static constexpr int kTileC = 2;
+static constexpr int kTileR = 4;
 
 template <int DT>
-__device__ __forceinline__ uint32_t t2_ld(uint64_t p, int dt, int64_t off) {
-  const int d = DT >= 0 ? DT : dt;
-  if (d == kF32) return reinterpret_cast<const uint32_t*>(p)[off];
-  return reinterpret_cast<const uint16_t*>(p)[off];
+__device__ __forceinline__ int t2_esz(int dt) {
+  return (DT >= 0 ? DT : dt) == kF32 ? 4 : 2;
+}
+
+template <int DT>
+__device__ __forceinline__ uint32_t t2_ld(const uint8_t* p, int dt) {
+  if ((DT >= 0 ? DT : dt) == kF32) return *reinterpret_cast<const uint32_t*>(p);
+  return *reinterpret_cast<const uint16_t*>(p);
 }
 
 template <int DT>
@@ -286,8 +294,8 @@ __device__ __forceinline__ float t2_cvt(uint32_t r, int dt) {
 }
 
 template <int DT>
-__device__ __forceinline__ void t2_st(uint64_t p, int dt, int64_t off, float v) {
-  st1(p, DT >= 0 ? DT : dt, off, v);
+__device__ __forceinline__ void t2_st(uint8_t* p, int dt, float v) {
+  st1(reinterpret_cast<uint64_t>(p), DT >= 0 ? DT : dt, 0, v);
 }
 
 template <int V>
@@ -309,37 +317,60 @@ __device__ __forceinline__ void ew_tile2d(const ReqView& q, int v, float p0, flo
   const int64_t ce = min(N, cb + (int64_t)q.chunk);
   const bool hasb = q.flags & RF_HAS_B;
   const bool a_sc = q.flags & RF_A_SCALAR, b_sc = q.flags & RF_B_SCALAR;
-  const int64_t sar = q.sa_row, sai = q.sa_in, sbr = q.sb_row, sbi = q.sb_in, sor = q.so_row;
-  // per-row B that does not vary along the row ([B,1]): one value per row, the
-  // same for every lane; per-column B that does not vary down the rows ([N]):
-  // one value per lane and column
-  const bool b_col = hasb && !b_sc && sbr == 0;
+  const int ea = t2_esz<DA>(q.dta), eb = t2_esz<DB>(q.dtb), eo = t2_esz<DO>(q.dto);
+  // byte strides down the rows (0 for a scalar operand)
+  const int64_t ra_b = a_sc ? 0 : q.sa_row * ea, rb_b = b_sc ? 0 : q.sb_row * eb;
+  const int64_t ro_b = q.so_row * eo;
+  // B that does not vary down the rows ([N]) or at all: one value per column
+  const bool b_col = hasb && (b_sc || q.sb_row == 0);
 #pragma unroll 1
-  for (int64_t c = cb + lane; c < ce; c += 32) {
-    const int64_t ao = a_sc ? 0 : c * sai;
-    const int64_t bo = b_sc ? 0 : c * sbi;
-    const float bcol = (hasb && (b_col || b_sc)) ? t2_cvt<DB>(t2_ld<DB>(q.b, q.dtb, bo), q.dtb) : 0.f;
-#pragma unroll 1
-    for (int64_t i0 = 0; i0 < R; i0 += kTileU) {
-      uint32_t ra[kTileU], rb[kTileU];
+  for (int64_t c0 = cb + lane; c0 < ce; c0 += 32 * kTileC) {
+    const uint8_t* pa[kTileC];
+    const uint8_t* pb[kTileC];
+    uint8_t* po[kTileC];
+    float bc[kTileC];
+    bool ok[kTileC];
 #pragma unroll
-      for (int u = 0; u < kTileU; ++u) {
-        ra[u] = 0u;
-        rb[u] = 0u;
-        const int64_t i = i0 + u;
-        if (i < R) {
-          ra[u] = t2_ld<DA>(q.a, q.dta, a_sc ? 0 : ao + i * sar);
-          if (hasb && !b_col && !b_sc) rb[u] = t2_ld<DB>(q.b, q.dtb, bo + i * sbr);
+    for (int j = 0; j < kTileC; ++j) {
+      const int64_t c = c0 + 32 * j;
+      ok[j] = c < ce;
+      const int64_t cc = ok[j] ? c : c0;  // an in-range column keeps the pointers valid
+      pa[j] = reinterpret_cast<const uint8_t*>(q.a) + (a_sc ? 0 : cc * q.sa_in * ea);
+      pb[j] = reinterpret_cast<const uint8_t*>(q.b) + (b_sc ? 0 : cc * q.sb_in * eb);
+      po[j] = reinterpret_cast<uint8_t*>(q.o) + cc * eo;
+      bc[j] = b_col ? t2_cvt<DB>(t2_ld<DB>(pb[j], q.dtb), q.dtb) : 0.f;
+    }
+#pragma unroll 1
+    for (int64_t i0 = 0; i0 < R; i0 += kTileR) {
+      uint32_t ra[kTileR][kTileC], rb[kTileR][kTileC];
+#pragma unroll
+      for (int u = 0; u < kTileR; ++u) {
+#pragma unroll
+        for (int j = 0; j < kTileC; ++j) {
+          ra[u][j] = 0u;
+          rb[u][j] = 0u;
+          if (ok[j] && i0 + u < R) {
+            ra[u][j] = t2_ld<DA>(pa[j] + u * ra_b, q.dta);
+            if (hasb && !b_col) rb[u][j] = t2_ld<DB>(pb[j] + u * rb_b, q.dtb);
+          }
         }
       }
 #pragma unroll
-      for (int u = 0; u < kTileU; ++u) {
-        const int64_t i = i0 + u;
-        if (i < R) {
-          const float A = t2_cvt<DA>(ra[u], q.dta);
-          const float B = hasb ? ((b_col || b_sc) ? bcol : t2_cvt<DB>(rb[u], q.dtb)) : 0.f;
-          t2_st<DO>(q.o, q.dto, i * sor + c, t2_op<V>(v, A, B, p0, p1));
+      for (int u = 0; u < kTileR; ++u) {
+#pragma unroll
+        for (int j = 0; j < kTileC; ++j) {
+          if (ok[j] && i0 + u < R) {
+            const float A = t2_cvt<DA>(ra[u][j], q.dta);
+            const float B = hasb ? (b_col ? bc[j] : t2_cvt<DB>(rb[u][j], q.dtb)) : 0.f;
+            t2_st<DO>(po[j] + u * ro_b, q.dto, t2_op<V>(v, A, B, p0, p1));
+          }
         }
+      }
+#pragma unroll
+      for (int j = 0; j < kTileC; ++j) {
+        pa[j] += kTileR * ra_b;
+        pb[j] += kTileR * rb_b;
+        po[j] += kTileR * ro_b;
       }
     }
   }
@@ -1002,10 +1033,21 @@ __device__ __forceinline__ void red_generic_warp(const Exec& ex, const ReqView& 
 // ---------------------------------------------------------------------------
 // One chunk of one request.
 // ---------------------------------------------------------------------------
+// The bodies a kernel carries: a batch of only elementwise or only reduction
+// requests runs a kernel with just those bodies (less code to fetch, fewer
+// registers, more resident warps); mixed batches and the persistent worker
+// carry both.
+enum Bodies : int { BODY_EW = 1, BODY_RED = 2, BODY_ALL = 3 };
+
 // `x` is the request's ExtRec, copied to shared memory (strided layouts only).
+template <int BODIES>
 __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, int v, float p0,
                                               float p1, uint32_t k, const ExtRec* x) {
   if (q.kind == RK_EW) {
+    if constexpr (!(BODIES & BODY_EW)) {
+      if (ex.lane == 0) set_err(ex, ERR_BAD_KIND);
+      return;
+    }
     if (!ew_known(v)) {
       if (ex.lane == 0) set_err(ex, ERR_BAD_OP);
       return;
@@ -1024,6 +1066,10 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
   // the kernel for custom expressions runs elementwise batches only
   if (ex.lane == 0) set_err(ex, ERR_BAD_KIND);
 #else
+  if constexpr (!(BODIES & BODY_RED)) {
+    if (ex.lane == 0) set_err(ex, ERR_BAD_KIND);
+    return;
+  }
   if (v != V_SUM && v != V_MEAN) {
     if (ex.lane == 0) set_err(ex, v < 0 ? ERR_BAD_OP : ERR_BAD_KIND);
     return;

@@ -33,10 +33,12 @@ gpuos_lean_kernel(const __grid_constant__ LeanBatch<N> bt) {
 }
 
 // The batch's descriptors are in the device staging ring (payload); its
-// counters are `st`, one slot of a device array.
-extern "C" __global__ void __launch_bounds__(kCtaThreads, kMinCtasPerSm)
-gpuos_batch_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
-                   volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
+// counters are `st`, one slot of a device array.  BODIES selects the chunk
+// bodies the kernel carries (process_chunk).
+template <int BODIES>
+__device__ __forceinline__ void batch_body(const uint8_t* payload, const BatchHdr& hdr,
+                                           BatchState* st, volatile uint64_t* done_ring,
+                                           uint64_t wait_limit_ns) {
   __shared__ ExtRec ext[kWarpsPerCta];
   __shared__ uint32_t cta_chunks;
   __shared__ StageSync ss;
@@ -48,12 +50,33 @@ gpuos_batch_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
   __syncthreads();
   const Exec ex = bind_batch(payload, hdr, st, done_ring, nullptr, wait_limit_ns);
   const int warp = threadIdx.x >> 5;
-  const uint32_t count = warp_batch(ex, blockIdx.x * kWarpsPerCta + warp,
-                                    gridDim.x * kWarpsPerCta, &ext[warp], &ss);
+  const uint32_t count = warp_batch<BODIES>(ex, blockIdx.x * kWarpsPerCta + warp,
+                                            gridDim.x * kWarpsPerCta, &ext[warp], &ss);
   // without stage barriers nothing waits on the batch's counters: the kernel's
   // completion completes the batch, and its warps leave as soon as they are done
   if (posts_own_errors(ex)) return;
   cta_leave_batch(ex, &cta_chunks, count, gridDim.x, nullptr);
+}
+
+extern "C" __global__ void __launch_bounds__(kCtaThreads, kMinCtasPerSm)
+gpuos_batch_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
+                   volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
+  batch_body<BODY_ALL>(payload, hdr, st, done_ring, wait_limit_ns);
+}
+
+// Batches of only elementwise requests (that the lean kernel does not take)
+// and of only reductions: the same loop with one class of bodies (less code
+// to fetch); the reduction bodies need fewer registers, so 3 CTAs per SM.
+extern "C" __global__ void __launch_bounds__(kCtaThreads, kMinCtasPerSm)
+gpuos_batch_ew_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
+                      volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
+  batch_body<BODY_EW>(payload, hdr, st, done_ring, wait_limit_ns);
+}
+
+extern "C" __global__ void __launch_bounds__(kCtaThreads, 3)
+gpuos_batch_red_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
+                       volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
+  batch_body<BODY_RED>(payload, hdr, st, done_ring, wait_limit_ns);
 }
 
 // Copy `bytes` (multiple of 16, both ends 16-byte aligned) from mapped host
@@ -181,8 +204,8 @@ __device__ __forceinline__ void worker_loop(const WorkerArgs& w, CtaSmem* sm) {
       if (ex.flags & BF_AFTER_PREV) wait_prev_batches(ex);
     }
     __syncthreads();
-    const uint32_t count = warp_batch(ex, gw, nproc * kWarpsPerCta, &sm->ext[threadIdx.x >> 5],
-                                      &sm->ss);
+    const uint32_t count = warp_batch<BODY_ALL>(ex, gw, nproc * kWarpsPerCta,
+                                                &sm->ext[threadIdx.x >> 5], &sm->ss);
     cta_leave_batch(ex, &sm->chunks, count, nproc, w.retired_ring);
   }
 }
@@ -201,9 +224,17 @@ extern "C" int gpuos_cta_threads() { return gpuos::kCtaThreads; }
 
 extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::BatchHdr* hdr,
                                           gpuos::BatchState* st, volatile uint64_t* done_ring,
-                                          uint64_t wait_limit_ns, int grid, cudaStream_t stream) {
-  gpuos::gpuos_batch_kernel<<<grid, gpuos::kCtaThreads, 0, stream>>>(payload, *hdr, st, done_ring,
-                                                                     wait_limit_ns);
+                                          uint64_t wait_limit_ns, int grid, cudaStream_t stream,
+                                          int bodies) {
+  if (bodies == gpuos::BODY_EW)
+    gpuos::gpuos_batch_ew_kernel<<<grid, gpuos::kCtaThreads, 0, stream>>>(payload, *hdr, st,
+                                                                          done_ring, wait_limit_ns);
+  else if (bodies == gpuos::BODY_RED)
+    gpuos::gpuos_batch_red_kernel<<<grid, gpuos::kCtaThreads, 0, stream>>>(payload, *hdr, st,
+                                                                           done_ring, wait_limit_ns);
+  else
+    gpuos::gpuos_batch_kernel<<<grid, gpuos::kCtaThreads, 0, stream>>>(payload, *hdr, st, done_ring,
+                                                                       wait_limit_ns);
   return cudaGetLastError();
 }
 
@@ -253,9 +284,16 @@ extern "C" size_t gpuos_lean_params_size(int size_class) {
 
 // Resident blocks per SM of the two kernels (the persistent grid must be
 // fully resident).
-extern "C" cudaError_t gpuos_occupancy(int* batch_blocks_per_sm, int* worker_blocks_per_sm) {
+extern "C" cudaError_t gpuos_occupancy(int* batch_blocks_per_sm, int* worker_blocks_per_sm,
+                                       int* ew_blocks_per_sm, int* red_blocks_per_sm) {
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
       batch_blocks_per_sm, gpuos::gpuos_batch_kernel, gpuos::kCtaThreads, 0);
+  if (e != cudaSuccess) return e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(ew_blocks_per_sm, gpuos::gpuos_batch_ew_kernel,
+                                                    gpuos::kCtaThreads, 0);
+  if (e != cudaSuccess) return e;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(red_blocks_per_sm, gpuos::gpuos_batch_red_kernel,
+                                                    gpuos::kCtaThreads, 0);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(
       worker_blocks_per_sm, gpuos::gpuos_worker_kernel, gpuos::kCtaThreads, 0);

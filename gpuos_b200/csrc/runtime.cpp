@@ -22,9 +22,11 @@
 
 extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::BatchHdr* hdr,
                                           gpuos::BatchState* st, volatile uint64_t* done_ring,
-                                          uint64_t wait_limit_ns, int grid, cudaStream_t stream);
+                                          uint64_t wait_limit_ns, int grid, cudaStream_t stream,
+                                          int bodies);
 extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, cudaStream_t stream);
-extern "C" cudaError_t gpuos_occupancy(int* batch_blocks_per_sm, int* worker_blocks_per_sm);
+extern "C" cudaError_t gpuos_occupancy(int* batch_blocks_per_sm, int* worker_blocks_per_sm,
+                                       int* ew_blocks_per_sm, int* red_blocks_per_sm);
 extern "C" int gpuos_cta_threads();
 extern "C" cudaError_t gpuos_launch_lean(const void* params, int size_class, int grid,
                                          cudaStream_t stream);
@@ -366,7 +368,10 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   // accepted for API compatibility.
   block_ = gpuos_cta_threads();
   int bbps = 0, wbps = 0;
-  GCU(gpuos_occupancy(&bbps, &wbps));
+  int ebps = 0, rbps = 0;
+  GCU(gpuos_occupancy(&bbps, &wbps, &ebps, &rbps));
+  ew_bps_ = std::max(1, ebps);
+  red_bps_ = std::max(1, rbps);
   if (bbps < 1 || wbps < 2) throw GError(GPUOS_ECUDA, "batch CTAs cannot be resident");
   batch_bps_ = bbps;
   // the persistent grid is fully resident: CTA 0 stages batches, the rest run them
@@ -682,7 +687,8 @@ void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
       q.flags |= RF_VEC;
       const int64_t GE = 16 / e;
       const uint32_t rg = (uint32_t)(32 * GE);
-      int64_t seglen = std::max<int64_t>(8, 16384 / rg);
+      // about 8192 elements a chunk, as a contiguous row chunk holds
+      int64_t seglen = std::max<int64_t>(8, kSeg / rg);
       int64_t nseg = std::max<int64_t>(1, (C + seglen - 1) / seglen);
       if (nseg > 256) {
         seglen = (C + 255) / 256;
@@ -1121,12 +1127,13 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   }
   cb[n] = (uint32_t)nchunk;
   if (nchunk > 0xffffffffull) throw GError(GPUOS_EINVAL, "batch too large");
-  // Granules: the unit of work a warp takes at a time, about two per warp
-  // (at most 8 chunks each).
+  // Granules: the unit of work a warp takes at a time, about eight per warp
+  // (at most 8 chunks each): chunks of different requests cost different
+  // times, and more granules per warp even out the warps' totals.
   // (a batch with stage barriers: one chunk each, so that a stage spreads
   // over as many warps as it has chunks)
   const uint64_t warps_all = (uint64_t)std::max(1, total_warps_);
-  uint64_t gran = staged ? 1 : nchunk / (2 * warps_all);
+  uint64_t gran = staged ? 1 : nchunk / (8 * warps_all);
   gran = std::min<uint64_t>(std::max<uint64_t>(gran, 1), 8);
   const uint64_t ngran = (nchunk + gran - 1) / gran;
   const uint64_t rec_off = sizeof(BatchHdr);
@@ -1269,8 +1276,13 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     } else {
       GCU(cudaMemcpyAsync(ring_ + aoff, arena_ + aoff, bytes, cudaMemcpyHostToDevice, stream));
     }
+    // a batch of one class of requests runs the kernel with only those bodies
+    int bodies = 0;
+    for (uint32_t r = 0; r < n; ++r) bodies |= reqs[i + r].r.kind == RK_EW ? 1 : 2;
+    const int bps = bodies == 1 ? ew_bps_ : bodies == 2 ? red_bps_ : batch_bps_;
     const uint64_t wpc = (uint64_t)block_ / 32;
-    int grid = (int)std::min<uint64_t>((uint64_t)sm_count_ * batch_bps_, (ngran + wpc - 1) / wpc);
+    int grid = (int)std::min<uint64_t>((uint64_t)sm_count_ * (jit_batch ? batch_bps_ : bps),
+                                       (ngran + wpc - 1) / wpc);
     grid = std::max(grid, 1);
     volatile uint64_t* dr = reinterpret_cast<volatile uint64_t*>(
         hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));
@@ -1291,7 +1303,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
                  states_ + seq % kDoneRing, dr, wait_limit_ns_);
     } else {
       GCU(gpuos_launch_batch(ring_ + aoff, h, states_ + seq % kDoneRing, dr, wait_limit_ns_, grid,
-                             stream));
+                             stream, bodies));
     }
     if (timing_) {
       GCU(cudaEventRecord(e1, stream));

@@ -161,6 +161,7 @@ class Executor {
   int block_ = 512;
   int grid_ = 0;                // persistent worker grid (ingest CTA included)
   int batch_bps_ = 1;           // stream kernel: resident blocks per SM
+  int ew_bps_ = 1, red_bps_ = 1;  // the same for the elementwise-only / reduction-only kernels
   int total_warps_ = 1;         // warps that execute a batch (chunk sizing)
   uint64_t idle_ns_ = 0, wait_limit_ns_ = 0;
   double sync_timeout_s_ = 60.0;

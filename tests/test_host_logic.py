@@ -134,11 +134,11 @@ def test_plan_reductions():
     p = C.plan_reduce(C.variant("mean"), xt, torch.empty(100), [1], False)
     # rows adjacent and 16-byte aligned: lanes read 16 bytes of 4 rows (128 per group)
     assert (p["layout"], p["sa_row"], p["sa_in"], p["rg"]) == (1, 1, 100, 128)
-    assert p["flags"] & 2 and p["chunk"] == 128 and p["nseg"] == 24
-    assert p["nchunk"] == 24 and p["partials"] == 24 * 128 and p["counters"] == 1
+    assert p["flags"] & 2 and p["chunk"] == 64 and p["nseg"] == 47
+    assert p["nchunk"] == 47 and p["partials"] == 47 * 128 and p["counters"] == 1
     xb = torch.randn(3000, 256, dtype=torch.bfloat16).t()    # bf16: 8 rows per lane
     p = C.plan_reduce(C.variant("sum"), xb, torch.empty(256, dtype=torch.bfloat16), [1], False)
-    assert p["flags"] & 2 and p["rg"] == 256 and p["chunk"] == 64
+    assert p["flags"] & 2 and p["rg"] == 256 and p["chunk"] == 32
     xo = torch.randn(3000, 99).t()                              # 99 rows: not a multiple of 4
     p = C.plan_reduce(C.variant("mean"), xo, torch.empty(99), [1], False)
     assert (p["layout"], p["rg"]) == (1, 32) and not p["flags"] & 2
