@@ -56,6 +56,7 @@ SIGNATURES = {
     "gpuos_submit_builtin": (ctypes.c_int32, [_VP, ctypes.c_int32, P(Tensor), P(Tensor), P(Tensor)]),
     "gpuos_submit_unary": (ctypes.c_int32, [_VP, ctypes.c_int32, P(Tensor), P(Tensor)]),
     "gpuos_submit_binary": (ctypes.c_int32, [_VP, ctypes.c_int32, P(Tensor), P(Tensor), P(Tensor)]),
+    "gpuos_submit_nary": (ctypes.c_int32, [_VP, ctypes.c_int32, ctypes.c_int32, P(Tensor), P(Tensor)]),
     "gpuos_register_elementwise": (ctypes.c_int32, [_VP, ctypes.c_char_p, ctypes.c_char_p,
                                                     ctypes.c_int32, P(ctypes.c_int32)]),
     "gpuos_register_reduce": (ctypes.c_int32, [_VP, ctypes.c_char_p, ctypes.c_char_p,
@@ -217,6 +218,11 @@ class Executor:
     def binary(self, slot, a, b, out):
         check(lib().gpuos_submit_binary(self.h, slot, ctypes.byref(tensor(a)),
                                         ctypes.byref(tensor(b)), ctypes.byref(tensor(out))))
+
+    def nary(self, slot, inputs, out):
+        """out = expr(A, B, C, D) of slot `slot` over 1 to 4 input tensors."""
+        arr = (Tensor * len(inputs))(*[tensor(t) for t in inputs])
+        check(lib().gpuos_submit_nary(self.h, slot, len(inputs), arr, ctypes.byref(tensor(out))))
 
     def register_elementwise(self, key, expr, arity) -> int:
         s = ctypes.c_int32()

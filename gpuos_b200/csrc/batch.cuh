@@ -66,7 +66,8 @@ struct Cur {
 
 // The record carries the operator the request's slot named when it was
 // flushed (the host resolves the jump table), and its parameters.  A strided
-// request's ExtRec is copied from the arena to the warp's shared-memory slot.
+// (or more-operand) request's ExtRec is copied from the arena to the warp's
+// shared-memory slot.
 // `words`: the record as load_req_words returned it (loaded ahead of time).
 __device__ __forceinline__ void decode(Cur& cur, const Exec& ex, const Req* rec, uint4 words,
                                        ExtRec* xs) {
@@ -91,10 +92,11 @@ __device__ __forceinline__ void decode(Cur& cur, const Exec& ex, const Req* rec,
       cur.v = V_NONE;
     }
   }
-  cur.vec = q.kind == RK_EW && (q.flags & RF_VEC) && q.layout != EL_STRIDED && ew_known(cur.v);
+  cur.vec = q.kind == RK_EW && (q.flags & RF_VEC) && !(q.flags & RF_NARY) &&
+            q.layout != EL_STRIDED && ew_known(cur.v);
   if (cur.vec) {
     cur.u = vec_view(q);
-  } else if ((q.kind == RK_EW && q.layout == EL_STRIDED) ||
+  } else if ((q.kind == RK_EW && (q.layout == EL_STRIDED || (q.flags & RF_NARY))) ||
              (q.kind == RK_RED && q.layout == RL_GENERIC)) {
     static_assert(sizeof(ExtRec) % 16 == 0, "ExtRec is copied in 16-byte words");
     const uint4* src = reinterpret_cast<const uint4*>(ex.base + q.ext);
@@ -132,6 +134,7 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
   const int lane = ex.lane;
   const uint32_t nchunk = ex.nchunk;
   const bool staged = ex.flags & BF_STAGED;
+  const bool dyn = ex.flags & (BF_STAGED | BF_CLAIM);  // granules claimed one at a time
   const uint32_t G = ex.gran;
   const uint32_t ngran = G ? (nchunk + G - 1) / G : 0u;
   auto claim = [&]() -> uint32_t {
@@ -139,12 +142,12 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
     if (lane == 0) x = atomicAdd(&ex.st->claim, 1u);
     return __shfl_sync(GPUOS_FULL, x, 0);
   };
-  // Without stage barriers warp gw takes the contiguous granule range
-  // [gw G / W, (gw + 1) G / W): requests are sorted by operator, so the warps
-  // of an SM run one or two operator bodies at a time.  With stage barriers
-  // granules are claimed in order.
+  // Otherwise warp gw takes the contiguous granule range [gw G / W,
+  // (gw + 1) G / W): requests are sorted by operator, so the warps of an SM
+  // run one or two operator bodies at a time.  With stage barriers granules
+  // are claimed in order.
   uint32_t j, jend = ngran;
-  if (staged) {
+  if (dyn) {
     j = claim();
   } else {
     j = (uint32_t)((uint64_t)gw * ngran / W);
@@ -164,7 +167,7 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
   uint2 gq = make_uint2(0u, 0u);
   if (j < jend) {
     g = __ldcg(ex.gtab + j);
-    if (!staged) {
+    if (!dyn) {
       const uint32_t jq = next_of(j);
       if (jq < ngran) gq = __ldcg(ex.gtab + jq);
     }
@@ -172,9 +175,9 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
     g_end = __ldcg(ex.gcb + g.x + 1);
   }
   while (j < jend) {
-    const uint32_t jn = staged ? claim() : next_of(j);  // the next granule, known ahead
+    const uint32_t jn = dyn ? claim() : next_of(j);  // the next granule, known ahead
     uint2 gn;
-    if (staged) {
+    if (dyn) {
       gn = jn < ngran ? __ldcg(ex.gtab + jn) : make_uint2(0u, 0u);
     } else {
       gn = gq;

@@ -175,12 +175,13 @@ struct Exec {
   int lane;
 };
 
-// A stream-mode batch without stage barriers has no end-of-batch protocol
-// (the event recorded after its launch completes it), so an error is posted
-// to the host at once: the completion word with the bits this warp knows; the
-// host reads the batch's full error bits from `st` after the kernel.
+// A stream-mode batch without stage barriers or claimed granules has no
+// end-of-batch protocol (the event recorded after its launch completes it),
+// so an error is posted to the host at once: the completion word with the
+// bits this warp knows; the host reads the batch's full error bits from `st`
+// after the kernel.
 __device__ __forceinline__ bool posts_own_errors(const Exec& ex) {
-  return !ex.done_dev && !(ex.flags & BF_STAGED);
+  return !ex.done_dev && !(ex.flags & (BF_STAGED | BF_CLAIM));
 }
 
 __device__ __forceinline__ void set_err(const Exec& ex, uint32_t bits) {
@@ -259,6 +260,84 @@ __device__ __forceinline__ void ew_generic(const ReqView& q, const ExtRec* x, in
     }
   }
 }
+
+#ifdef GPUOS_JIT_LINK
+// The general body for a custom expression of three or four operands
+// (RF_NARY): A and B as in ew_generic, C and D from the extension record.
+// The same rounds of K elements per lane, every load of a round issued
+// before any element is computed.
+__device__ __forceinline__ void ew_generic_nary(const ReqView& q, const ExtRec* x, int v,
+                                                float p0, float p1, int64_t e0, int64_t e1,
+                                                int lane) {
+  constexpr int K = 4;
+  const bool hasb = q.flags & RF_HAS_B;
+  const bool hasd = x->d != 0;
+  const int lay = q.layout;
+  const int64_t N = q.inner;
+#pragma unroll 1
+  for (int64_t eb = e0 + lane; eb < e1; eb += 32 * K) {
+    uint32_t ra[K], rb[K], rc[K], rd[K];
+    int64_t oo[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t e = eb + 32 * k;
+      ra[k] = rb[k] = rc[k] = rd[k] = 0u;
+      oo[k] = 0;
+      if (e < e1) {
+        int64_t oa, ob, oc, od;
+        if (lay == EL_CONTIG) {
+          oa = (q.flags & RF_A_SCALAR) ? 0 : e;
+          ob = (q.flags & RF_B_SCALAR) ? 0 : e;
+          oc = e * x->sc[0];
+          od = e * x->sd[0];
+          oo[k] = e;
+        } else if (lay == EL_ROW2D) {
+          const int64_t r = row_of(q, e), c = e - r * N;
+          oa = r * q.sa_row + c * q.sa_in;
+          ob = r * q.sb_row + c * q.sb_in;
+          oc = r * x->sc[0] + c * x->sc[1];
+          od = r * x->sd[0] + c * x->sd[1];
+          oo[k] = r * q.so_row + c;
+        } else {
+          int64_t rem = e, o = 0;
+          oa = ob = oc = od = 0;
+          for (int d = x->ndim - 1; d >= 0; --d) {
+            const int64_t sz = x->sizes[d];
+            const int64_t i = rem % sz;
+            rem /= sz;
+            oa += i * x->sa[d];
+            ob += i * x->sb[d];
+            oc += i * x->sc[d];
+            od += i * x->sd[d];
+            o += i * x->so[d];
+          }
+          oo[k] = o;
+        }
+        ra[k] = ld1_raw(q.a, q.dta, oa);
+        if (hasb) rb[k] = ld1_raw(q.b, q.dtb, ob);
+        rc[k] = ld1_raw(x->c, x->dtc, oc);
+        if (hasd) rd[k] = ld1_raw(x->d, x->dtd, od);
+      }
+    }
+    const int nk = (int)min((int64_t)K, (e1 - eb + 31) / 32);
+#pragma unroll 1
+    for (int k = 0; k < nk; ++k) {
+      float R = 0.f;
+      ew_apply4(v, cvt1(ra[0], q.dta), hasb ? cvt1(rb[0], q.dtb) : 0.f, cvt1(rc[0], x->dtc),
+                hasd ? cvt1(rd[0], x->dtd) : 0.f, R, p0, p1);
+      st1(q.o, q.dto, oo[0], R);
+#pragma unroll
+      for (int j = 0; j + 1 < K; ++j) {
+        ra[j] = ra[j + 1];
+        rb[j] = rb[j + 1];
+        rc[j] = rc[j + 1];
+        rd[j] = rd[j + 1];
+        oo[j] = oo[j + 1];
+      }
+    }
+  }
+}
+#endif
 
 // ---------------------------------------------------------------------------
 // 2-D elementwise tiles (EL_TILE2D): a chunk is a block of `chunk` columns of
@@ -673,83 +752,97 @@ __device__ __forceinline__ bool combine_arrive(const Exec& ex, uint32_t* cnt, ui
 }
 
 // Rows contiguous: a lane group of q.rg lanes sums one row (nseg == 1), or the
-// whole warp sums one segment of a long row (nseg > 1).
-// Sum of the elements [c, c + n) of one row, `stride` lanes apart: lane i of
-// the group adds elements i, i + stride, ...  Raw loads, kRedU of them in
-// flight per lane, converted and added after they are all issued.
-static constexpr int kRedU = 8;
-
-__device__ __forceinline__ void red_span_scalar(const ReqView& q, int64_t base, int64_t c,
-                                                int64_t c1, int stride, float& acc0,
-                                                float& acc1) {
-#pragma unroll 1
-  for (; c < c1; c += (int64_t)stride * kRedU) {
-    uint32_t w[kRedU];
-#pragma unroll
-    for (int u = 0; u < kRedU; ++u) {
-      w[u] = 0u;
-      if (c + (int64_t)stride * u < c1) w[u] = ld1_raw(q.a, q.dta, base + c + (int64_t)stride * u);
-    }
-#pragma unroll
-    for (int u = 0; u < kRedU; ++u)
-      if (c + (int64_t)stride * u < c1) (u & 1 ? acc1 : acc0) += cvt1(w[u], q.dta);
-  }
-}
-
-// The same over 16-byte groups (4 fp32 or 8 fp16 / bf16 elements) starting
-// at c + GE i, c + GE (i + stride), ... up to cg (a multiple of GE elements
-// past c, GE = 16 / element size); kRedVU groups in flight per lane.
+// whole warp sums one segment of a long row (nseg > 1).  A row (or segment)
+// is read in aligned 16-byte blocks, 4 fp32 or 8 fp16 / bf16 elements,
+// whatever the alignment of its first element: the blocks that cover the
+// span are loaded whole, and the elements of the first and last block that
+// lie outside the span are zeroed before they are added.  (A 16-byte block
+// that holds an element of the tensor lies in the same memory page, so the
+// whole-block load is always in bounds.)  Lane i of a group takes blocks i,
+// i + G, ..., kRedVU of them in flight, converted and added after all are
+// issued.
 static constexpr int kRedVU = 8;
 
-__device__ __forceinline__ void add16(uint4 w, int dt, float& acc0, float& acc1) {
-  if (dt == kF32) {
+template <int DT>
+__device__ __forceinline__ void add16_t(uint4 w, float& acc0, float& acc1) {
+  if constexpr (DT == kF32) {
     acc0 += __uint_as_float(w.x) + __uint_as_float(w.z);
     acc1 += __uint_as_float(w.y) + __uint_as_float(w.w);
-    return;
-  }
-  float v[8];
-  if (dt == kF16) {
-    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
-      v[2 * k] = f.x;
-      v[2 * k + 1] = f.y;
-    }
   } else {
-    bf2_to_f(w.x, v[0], v[1]);
-    bf2_to_f(w.y, v[2], v[3]);
-    bf2_to_f(w.z, v[4], v[5]);
-    bf2_to_f(w.w, v[6], v[7]);
+    float v[8];
+    if constexpr (DT == kF16) {
+      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
+        v[2 * k] = f.x;
+        v[2 * k + 1] = f.y;
+      }
+    } else {
+      bf2_to_f(w.x, v[0], v[1]);
+      bf2_to_f(w.y, v[2], v[3]);
+      bf2_to_f(w.z, v[4], v[5]);
+      bf2_to_f(w.w, v[6], v[7]);
+    }
+    acc0 += (v[0] + v[2]) + (v[4] + v[6]);
+    acc1 += (v[1] + v[3]) + (v[5] + v[7]);
   }
-  acc0 += (v[0] + v[2]) + (v[4] + v[6]);
-  acc1 += (v[1] + v[3]) + (v[5] + v[7]);
 }
 
-__device__ __forceinline__ void red_span_vec(const ReqView& q, int64_t base, int64_t c, int64_t cg,
-                                             int stride, float& acc0, float& acc1) {
-  const int GE = q.dta == kF32 ? 4 : 8;
-  const int64_t step = (int64_t)GE * stride;
-  const uint8_t* p = reinterpret_cast<const uint8_t*>(q.a);
-  const int es = q.dta == kF32 ? 4 : 2;
+// Zero the elements of the block at byte address `blk` that lie outside [s, e).
+template <int DT>
+__device__ __forceinline__ uint4 mask16_t(uint4 w, uint64_t blk, uint64_t s, uint64_t e) {
+  uint32_t v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint64_t a = blk + 4 * j;
+    if constexpr (DT == kF32) {
+      if (a < s || a >= e) v[j] = 0u;
+    } else {
+      uint32_t m = 0u;
+      if (a >= s && a < e) m |= 0x0000ffffu;
+      if (a + 2 >= s && a + 2 < e) m |= 0xffff0000u;
+      v[j] &= m;
+    }
+  }
+  return make_uint4(v[0], v[1], v[2], v[3]);
+}
+
+// Sum of the elements at byte addresses [s, e) of one span: lane li of G.
+template <int DT>
+__device__ __forceinline__ void red_span_t(uint64_t s, uint64_t e, int li, int G, float& acc0,
+                                           float& acc1) {
+  if (e <= s) return;
+  const uint64_t b0 = s & ~15ull;
+  const uint32_t nb = (uint32_t)((((e + 15) & ~15ull) - b0) >> 4);
+  const uint32_t step = (uint32_t)G;
 #pragma unroll 1
-  for (; c < cg; c += step * kRedVU) {
+  for (uint32_t i = (uint32_t)li; i < nb; i += step * kRedVU) {
     uint4 w[kRedVU];
 #pragma unroll
     for (int u = 0; u < kRedVU; ++u) {
+      const uint32_t bi = i + step * u;
       w[u] = make_uint4(0u, 0u, 0u, 0u);
-      if (c + step * u < cg) w[u] = *reinterpret_cast<const uint4*>(p + (base + c + step * u) * es);
+      if (bi < nb) w[u] = *reinterpret_cast<const uint4*>(b0 + 16ull * bi);
     }
 #pragma unroll
-    for (int u = 0; u < kRedVU; ++u)
-      if (c + step * u < cg) add16(w[u], q.dta, acc0, acc1);
+    for (int u = 0; u < kRedVU; ++u) {
+      const uint32_t bi = i + step * u;
+      if (bi < nb) {
+        uint4 x = w[u];
+        if (bi == 0 || bi == nb - 1) x = mask16_t<DT>(x, b0 + 16ull * bi, s, e);
+        add16_t<DT>(x, acc0, acc1);
+      }
+    }
   }
 }
 
-__device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool mean, uint32_t k) {
+template <int DT>
+__device__ __forceinline__ void red_rows_t(const Exec& ex, const ReqView& q, bool mean,
+                                           uint32_t k) {
+  constexpr int ES = DT == kF32 ? 4 : 2;
   const int lane = ex.lane;
   const int64_t C = q.inner;
-  const bool vec = q.flags & RF_VEC;
   if (q.nseg == 1) {
     const int G = (int)q.rg;                   // lanes per row (power of two)
     const int per = 32 / G;                    // rows per warp step
@@ -762,15 +855,8 @@ __device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool 
       const bool valid = r < r1;
       float acc0 = 0.f, acc1 = 0.f;
       if (valid) {
-        const int64_t base = r * q.sa_row;
-        if (vec) {
-          const int GE = q.dta == kF32 ? 4 : 8;
-          const int64_t CG = C & ~(int64_t)(GE - 1);
-          red_span_vec(q, base, (int64_t)GE * li, CG, G, acc0, acc1);
-          red_span_scalar(q, base, CG + li, C, G, acc0, acc1);
-        } else {
-          red_span_scalar(q, base, li, C, G, acc0, acc1);
-        }
+        const uint64_t s = q.a + (uint64_t)(r * q.sa_row * ES);
+        red_span_t<DT>(s, s + (uint64_t)(C * ES), li, G, acc0, acc1);
       }
       float acc = acc0 + acc1;
       for (int off = G >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(GPUOS_FULL, acc, off);
@@ -785,16 +871,9 @@ __device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool 
   const int64_t c0 = (int64_t)seg * q.chunk;
   int64_t c1 = c0 + q.chunk;
   if (c1 > C) c1 = C;
-  const int64_t base = r * q.sa_row;
+  const uint64_t rowp = q.a + (uint64_t)(r * q.sa_row * ES);
   float acc0 = 0.f, acc1 = 0.f;
-  if (vec) {  // c0 is a multiple of 8 (chunk is), c1 may end ragged on the last segment
-    const int GE = q.dta == kF32 ? 4 : 8;
-    const int64_t cg = c0 + ((c1 - c0) & ~(int64_t)(GE - 1));
-    red_span_vec(q, base, c0 + (int64_t)GE * lane, cg, 32, acc0, acc1);
-    red_span_scalar(q, base, cg + lane, c1, 32, acc0, acc1);
-  } else {
-    red_span_scalar(q, base, c0 + lane, c1, 32, acc0, acc1);
-  }
+  red_span_t<DT>(rowp + (uint64_t)(c0 * ES), rowp + (uint64_t)(c1 * ES), lane, 32, acc0, acc1);
   float acc = acc0 + acc1;
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(GPUOS_FULL, acc, off);
   float* part = ex.scratch + q.part + r * nseg;
@@ -811,10 +890,35 @@ __device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool 
   }
 }
 
+__device__ __forceinline__ void red_rows(const Exec& ex, const ReqView& q, bool mean, uint32_t k) {
+  if (q.dta == kF32) red_rows_t<kF32>(ex, q, mean, k);
+  else if (q.dta == kF16) red_rows_t<kF16>(ex, q, mean, k);
+  else red_rows_t<kBF16>(ex, q, mean, k);
+}
+
 // Rows adjacent in memory (a transposed view): lanes own rows, so every step
-// of the column loop reads rg adjacent rows of cl columns; kRedU columns per
-// lane are in flight (raw loads, converted after all are issued).
-__device__ __forceinline__ void red_cols(const Exec& ex, const ReqView& q, bool mean, uint32_t k) {
+// of the column loop reads rg adjacent rows of cl columns; kColU columns per
+// lane are in flight (raw loads, converted after all are issued), whole
+// rounds without bounds checks and one guarded round for the rest.
+static constexpr int kColU = 16;
+
+template <int DT>
+__device__ __forceinline__ uint32_t ldraw_t(const uint8_t* p) {
+  if constexpr (DT == kF32) return *reinterpret_cast<const uint32_t*>(p);
+  else return *reinterpret_cast<const uint16_t*>(p);
+}
+
+template <int DT>
+__device__ __forceinline__ float cvraw_t(uint32_t w) {
+  if constexpr (DT == kF32) return __uint_as_float(w);
+  else if constexpr (DT == kF16) return __half2float(__ushort_as_half((unsigned short)w));
+  else return __uint_as_float(w << 16);
+}
+
+template <int DT>
+__device__ __forceinline__ void red_cols_t(const Exec& ex, const ReqView& q, bool mean,
+                                           uint32_t k) {
+  constexpr int ES = DT == kF32 ? 4 : 2;
   const int lane = ex.lane;
   const int64_t C = q.inner, R = q.numel;
   const int rg = (int)q.rg, cl = 32 / rg;
@@ -829,19 +933,28 @@ __device__ __forceinline__ void red_cols(const Exec& ex, const ReqView& q, bool 
   if (c1 > C) c1 = C;
   float acc0 = 0.f, acc1 = 0.f;
   if (valid) {
-    const int64_t rb = r * q.sa_row;
-    const int64_t sc = q.sa_in;
+    const int64_t ls = q.sa_in * ES * cl;      // bytes between a lane's columns
+    int64_t c = c0 + ci;
+    const uint8_t* pc = reinterpret_cast<const uint8_t*>(q.a) + (r * q.sa_row + c * q.sa_in) * ES;
 #pragma unroll 1
-    for (int64_t c = c0 + ci; c < c1; c += (int64_t)cl * kRedU) {
-      uint32_t w[kRedU];
+    for (; c + (int64_t)cl * (kColU - 1) < c1; c += (int64_t)cl * kColU) {
+      uint32_t w[kColU];
 #pragma unroll
-      for (int u = 0; u < kRedU; ++u) {
+      for (int u = 0; u < kColU; ++u) w[u] = ldraw_t<DT>(pc + u * ls);
+      pc += ls * kColU;
+#pragma unroll
+      for (int u = 0; u < kColU; ++u) (u & 1 ? acc1 : acc0) += cvraw_t<DT>(w[u]);
+    }
+    if (c < c1) {
+      uint32_t w[kColU];
+#pragma unroll
+      for (int u = 0; u < kColU; ++u) {
         w[u] = 0u;
-        if (c + (int64_t)cl * u < c1) w[u] = ld1_raw(q.a, q.dta, rb + (c + (int64_t)cl * u) * sc);
+        if (c + (int64_t)cl * u < c1) w[u] = ldraw_t<DT>(pc + u * ls);
       }
 #pragma unroll
-      for (int u = 0; u < kRedU; ++u)
-        if (c + (int64_t)cl * u < c1) (u & 1 ? acc1 : acc0) += cvt1(w[u], q.dta);
+      for (int u = 0; u < kColU; ++u)
+        if (c + (int64_t)cl * u < c1) (u & 1 ? acc1 : acc0) += cvraw_t<DT>(w[u]);
     }
   }
   float acc = acc0 + acc1;
@@ -861,6 +974,12 @@ __device__ __forceinline__ void red_cols(const Exec& ex, const ReqView& q, bool 
     }
     if (lane == 0) *cnt = 0u;
   }
+}
+
+__device__ __forceinline__ void red_cols(const Exec& ex, const ReqView& q, bool mean, uint32_t k) {
+  if (q.dta == kF32) red_cols_t<kF32>(ex, q, mean, k);
+  else if (q.dta == kF16) red_cols_t<kF16>(ex, q, mean, k);
+  else red_cols_t<kBF16>(ex, q, mean, k);
 }
 
 // Rows adjacent in memory, vector form (RF_VEC on an RL_COLS request: the row
@@ -1059,6 +1178,17 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
     const int64_t e0 = (int64_t)k * q.chunk;
     int64_t e1 = e0 + q.chunk;
     if (e1 > q.numel) e1 = q.numel;
+#ifdef GPUOS_JIT_LINK
+    if (q.flags & RF_NARY) {
+      ew_generic_nary(q, x, v, p0, p1, e0, e1, ex.lane);
+      return;
+    }
+#else
+    if (q.flags & RF_NARY) {  // only custom expressions take more than two operands
+      if (ex.lane == 0) set_err(ex, ERR_BAD_KIND);
+      return;
+    }
+#endif
     ew_generic(q, x, v, p0, p1, e0, e1, ex.lane);
     return;
   }

@@ -388,6 +388,58 @@ PyObject* py_submit_binary(PyObject*, PyObject* const* args, Py_ssize_t n) {
   Py_RETURN_NONE;
 }
 
+// submit_nary(slot, inputs, out): a custom expression of 1 to 4 inputs (no
+// counterpart in the reference module, whose requests take two at most).
+PyObject* py_submit_nary(PyObject*, PyObject* const* args, Py_ssize_t n) {
+  if (n != 3) {
+    PyErr_SetString(PyExc_TypeError, "expected (slot, inputs, out)");
+    return nullptr;
+  }
+  const long slot = PyLong_AsLong(args[0]);
+  if (PyErr_Occurred()) return nullptr;
+  PyObject* seq = PySequence_Fast(args[1], "inputs must be a sequence of tensors");
+  if (!seq) return nullptr;
+  const Py_ssize_t nin = PySequence_Fast_GET_SIZE(seq);
+  if (nin < 1 || nin > 4) {
+    Py_DECREF(seq);
+    PyErr_SetString(PyExc_ValueError, "a request takes 1 to 4 inputs");
+    return nullptr;
+  }
+  gpuos_tensor ins[4], o;
+  int dout;
+  if (!fill_desc(args[2], &o, &dout, "out")) {
+    Py_DECREF(seq);
+    return nullptr;
+  }
+  static const char* names[4] = {"a", "b", "c", "d"};
+  for (Py_ssize_t k = 0; k < nin; ++k) {
+    int d;
+    if (!fill_desc(PySequence_Fast_GET_ITEM(seq, k), &ins[k], &d, names[k])) {
+      Py_DECREF(seq);
+      return nullptr;
+    }
+    if (d != dout) {
+      Py_DECREF(seq);
+      PyErr_SetString(PyExc_RuntimeError, "device mismatch");
+      return nullptr;
+    }
+  }
+  gpuos_executor* ex = executor_for(dout);
+  if (!ex) {
+    Py_DECREF(seq);
+    return nullptr;
+  }
+  const int32_t rc = gpuos_submit_nary(ex, (int32_t)slot, (int32_t)nin, ins, &o);
+  if (rc != GPUOS_OK) {
+    Py_DECREF(seq);
+    return raise_status(rc);
+  }
+  for (Py_ssize_t k = 0; k < nin; ++k) keep(dout, PySequence_Fast_GET_ITEM(seq, k));
+  keep(dout, args[2]);
+  Py_DECREF(seq);
+  Py_RETURN_NONE;
+}
+
 PyObject* py_submit_reduce(PyObject*, PyObject* const* args, Py_ssize_t n) {
   if (n != 5) {
     PyErr_SetString(PyExc_TypeError, "expected (slot, x, out, axes, keepdim)");
@@ -565,6 +617,8 @@ PyMethodDef kMethods[] = {
      "submit_unary(slot, a, out)"},
     {"submit_binary", (PyCFunction)(void (*)(void))py_submit_binary, METH_FASTCALL,
      "submit_binary(slot, a, b, out)"},
+    {"submit_nary", (PyCFunction)(void (*)(void))py_submit_nary, METH_FASTCALL,
+     "submit_nary(slot, inputs, out): a custom expression of 1 to 4 inputs"},
     {"register_reduce", py_register_reduce, METH_VARARGS, "register_reduce(key, 'sum'|'mean') -> slot"},
     {"submit_reduce", (PyCFunction)(void (*)(void))py_submit_reduce, METH_FASTCALL,
      "submit_reduce(slot, x, out, axes, keepdim)"},

@@ -82,6 +82,8 @@ enum ReqFlags : uint8_t {
   RF_A_SCALAR = 8,   // operand A is a single element broadcast everywhere
   RF_B_SCALAR = 16,  // operand B is a single element broadcast everywhere
   RF_BIG = 32,       // indices may exceed 2^31: use 64-bit index math
+  RF_NARY = 64,      // operands C (and D) from the extension record: a custom
+                     // expression of arity 3 or 4 (the general body only)
 };
 
 static constexpr int kMaxDims = 8;
@@ -124,10 +126,14 @@ struct alignas(16) Req {
 };
 static_assert(sizeof(Req) == 128, "Req must stay 128 bytes");
 
-// Extension record for EL_STRIDED and RL_GENERIC (placed after the records).
+// Extension record for EL_STRIDED, RL_GENERIC and RF_NARY requests (placed
+// after the records).
 // EW: dims 0..ndim-1 of the output with per-operand element strides.
 // RED: `ndim` outer (kept) dims followed by `rdim` reduced dims; sa holds the
 //      input strides, so the output strides (output may be non-contiguous).
+// RF_NARY: operands C and D (d == 0: none) with their strides in sc / sd:
+//      EL_CONTIG sc[0] (0 or 1), EL_ROW2D sc[0] row and sc[1] inner stride,
+//      EL_STRIDED sc[d] per dim.
 struct alignas(16) ExtRec {
   int32_t ndim;
   int32_t rdim;
@@ -135,9 +141,18 @@ struct alignas(16) ExtRec {
   int64_t sa[kMaxDims];
   int64_t sb[kMaxDims];
   int64_t so[kMaxDims];
-  int64_t rsizes[kMaxDims];
-  int64_t rstrides[kMaxDims];
+  union {
+    int64_t rsizes[kMaxDims];
+    int64_t sc[kMaxDims];
+  };
+  union {
+    int64_t rstrides[kMaxDims];
+    int64_t sd[kMaxDims];
+  };
+  uint64_t c, d;         // RF_NARY: device addresses of operands C and D
+  int32_t dtc, dtd;      // and their dtypes
 };
+static_assert(sizeof(ExtRec) == 416, "ExtRec layout");
 
 // Batch header at offset 0 of every batch payload.
 struct alignas(16) BatchHdr {
@@ -220,6 +235,8 @@ static constexpr int kDoneRing = 1024;
 enum BatchFlags : uint32_t {
   BF_STAGED = 1,      // per-request stage waits follow the chunk prefix array
   BF_AFTER_PREV = 2,  // do not start before the previous batch is done
+  BF_CLAIM = 4,       // warps claim granules one at a time (large batches, whose
+                      // chunks differ in cost), and the batch ends through its counters
 };
 
 // Publication record of one batch (mapped host memory, ring of kDoneRing).

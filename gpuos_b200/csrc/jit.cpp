@@ -85,13 +85,28 @@ void check_expression(const std::string& e) {
 }
 
 std::string ops_source(const std::vector<std::string>& exprs) {
+  // gpuos_keep_f32 / _f16 / _bf16: the value a fused chain's intermediate
+  // result would have had in memory.  fp32: an add of -0.0 (exact for every
+  // value) with an explicit rounding mode, which the code generator never
+  // contracts with the multiply that produced the value, so the product is
+  // rounded on its own as in the unfused chain; fp16 / bf16: the rounding of
+  // the store (cvt.rn).
   std::string s =
-      "// custom expressions of one executor, A and B the operands\n"
+      "// custom expressions of one executor, A..D the operands\n"
       "#define INFINITY __int_as_float(0x7f800000)\n"
-      "#define NAN __int_as_float(0x7fffffff)\n";
+      "#define NAN __int_as_float(0x7fffffff)\n"
+      "static __device__ __forceinline__ float gpuos_keep_f32(float x) {\n"
+      "  float y; asm(\"add.rn.f32 %0, %1, 0f80000000;\" : \"=f\"(y) : \"f\"(x)); return y;\n}\n"
+      "static __device__ __forceinline__ float gpuos_keep_f16(float x) {\n"
+      "  float y; asm(\"{ .reg .b16 h; cvt.rn.f16.f32 h, %1; cvt.f32.f16 %0, h; }\" "
+      ": \"=f\"(y) : \"f\"(x)); return y;\n}\n"
+      "static __device__ __forceinline__ float gpuos_keep_bf16(float x) {\n"
+      "  unsigned u; asm(\"{ .reg .b16 h, z; cvt.rn.bf16.f32 h, %1; mov.b16 z, 0; "
+      "mov.b32 %0, {z, h}; }\" : \"=r\"(u) : \"f\"(x)); return __uint_as_float(u);\n}\n";
   for (int k = 0; k < kJitSlots; ++k) {
     s += "extern \"C\" __device__ float gpuos_jit_op" + std::to_string(k) +
-         "(float A, float B, float p0, float p1) {\n  (void)A; (void)B; (void)p0; (void)p1;\n"
+         "(float A, float B, float C, float D, float p0, float p1) {\n"
+         "  (void)A; (void)B; (void)C; (void)D; (void)p0; (void)p1;\n"
          "  return (float)(";
     s += k < (int)exprs.size() ? exprs[k] : std::string("A");
     s += ");\n}\n";
@@ -216,7 +231,7 @@ void jit_unload(JitKernel& k) {
 extern "C" int32_t gpuos_jit_check(const char* expr, int32_t arity) {
   try {
     if (!expr) throw gpuos::GError(GPUOS_EINVAL, "expression is NULL");
-    if (arity != 1 && arity != 2) throw gpuos::GError(GPUOS_EINVAL, "arity must be 1 or 2");
+    if (arity < 1 || arity > 4) throw gpuos::GError(GPUOS_EINVAL, "arity must be 1 to 4");
     gpuos::jit_compile({std::string(expr)});
     return GPUOS_OK;
   } catch (const gpuos::GError& e) {

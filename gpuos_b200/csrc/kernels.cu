@@ -66,14 +66,15 @@ gpuos_batch_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
 
 // Batches of only elementwise requests (that the lean kernel does not take)
 // and of only reductions: the same loop with one class of bodies (less code
-// to fetch); the reduction bodies need fewer registers, so 3 CTAs per SM.
+// to fetch).  Both at 2 CTAs per SM: at 3 the reduction bodies spill (80
+// registers), and the spill-free 128-register form measured faster.
 extern "C" __global__ void __launch_bounds__(kCtaThreads, kMinCtasPerSm)
 gpuos_batch_ew_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
                       volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
   batch_body<BODY_EW>(payload, hdr, st, done_ring, wait_limit_ns);
 }
 
-extern "C" __global__ void __launch_bounds__(kCtaThreads, 3)
+extern "C" __global__ void __launch_bounds__(kCtaThreads, kMinCtasPerSm)
 gpuos_batch_red_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
                        volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
   batch_body<BODY_RED>(payload, hdr, st, done_ring, wait_limit_ns);

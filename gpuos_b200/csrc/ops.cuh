@@ -24,7 +24,8 @@ namespace gpuos {
 static constexpr int kJitOps = 16;
 #ifdef GPUOS_JIT_LINK
 extern "C" {
-#define GPUOS_JIT_DECL(k) __device__ float gpuos_jit_op##k(float A, float B, float p0, float p1);
+#define GPUOS_JIT_DECL(k) \
+  __device__ float gpuos_jit_op##k(float A, float B, float C, float D, float p0, float p1);
 GPUOS_JIT_DECL(0) GPUOS_JIT_DECL(1) GPUOS_JIT_DECL(2) GPUOS_JIT_DECL(3)
 GPUOS_JIT_DECL(4) GPUOS_JIT_DECL(5) GPUOS_JIT_DECL(6) GPUOS_JIT_DECL(7)
 GPUOS_JIT_DECL(8) GPUOS_JIT_DECL(9) GPUOS_JIT_DECL(10) GPUOS_JIT_DECL(11)
@@ -32,8 +33,8 @@ GPUOS_JIT_DECL(12) GPUOS_JIT_DECL(13) GPUOS_JIT_DECL(14) GPUOS_JIT_DECL(15)
 #undef GPUOS_JIT_DECL
 }
 template <int K>
-__device__ __forceinline__ float jit_op(float A, float B, float p0, float p1) {
-#define GPUOS_JIT_CALL(k) if constexpr (K == k) return gpuos_jit_op##k(A, B, p0, p1);
+__device__ __forceinline__ float jit_op(float A, float B, float C, float D, float p0, float p1) {
+#define GPUOS_JIT_CALL(k) if constexpr (K == k) return gpuos_jit_op##k(A, B, C, D, p0, p1);
   GPUOS_JIT_CALL(0) GPUOS_JIT_CALL(1) GPUOS_JIT_CALL(2) GPUOS_JIT_CALL(3)
   GPUOS_JIT_CALL(4) GPUOS_JIT_CALL(5) GPUOS_JIT_CALL(6) GPUOS_JIT_CALL(7)
   GPUOS_JIT_CALL(8) GPUOS_JIT_CALL(9) GPUOS_JIT_CALL(10) GPUOS_JIT_CALL(11)
@@ -46,7 +47,8 @@ __device__ __forceinline__ float jit_op(float A, float B, float p0, float p1) {
 template <int V>
 __device__ __forceinline__ float op1(float A, float B, float p0, float p1) {
 #ifdef GPUOS_JIT_LINK
-  if constexpr (V >= V_JIT_BASE && V < V_JIT_BASE + kJitOps) return jit_op<V - V_JIT_BASE>(A, B, p0, p1);
+  if constexpr (V >= V_JIT_BASE && V < V_JIT_BASE + kJitOps)
+    return jit_op<V - V_JIT_BASE>(A, B, 0.f, 0.f, p0, p1);
   else
 #endif
   if constexpr (V == V_ADD) return A + B;
@@ -102,6 +104,19 @@ __device__ __forceinline__ bool ew_apply1(int v, float A, float B, float& r, flo
     default: return false;
   }
 }
+
+#ifdef GPUOS_JIT_LINK
+// A custom expression of up to four operands (RF_NARY requests).
+#define GPUOS_CASE4(V) case V: r = jit_op<V - V_JIT_BASE>(A, B, C, D, p0, p1); return true;
+__device__ __forceinline__ bool ew_apply4(int v, float A, float B, float C, float D, float& r,
+                                          float p0, float p1) {
+  switch (v) {
+    GPUOS_ALL_EW(GPUOS_CASE4)
+    default: return false;
+  }
+}
+#undef GPUOS_CASE4
+#endif
 
 // Groups of 4 elements each lane handles per iteration of the vector loop
 // (the loop keeps the next iteration's loads in flight while it computes the

@@ -582,6 +582,117 @@ void build_ew(Pending& p, int op, bool is_slot, float p0, float p1,
   }
 }
 
+// A custom expression of three or four operands (RF_NARY): A and B in the
+// record, C and D in the extension record.  The general body runs it
+// (contiguous, [rows, inner] or up to 8 strided dims after broadcasting and
+// dim coalescing), without the vector or 2-D tile paths.
+void build_ew_nary(Pending& p, int op, bool is_slot, float p0, float p1,
+                   const gpuos_tensor* const* ins, int nin, const gpuos_tensor& out) {
+  static const char* names[4] = {"input A", "input B", "input C", "input D"};
+  if (nin < 3 || nin > 4) throw GError(GPUOS_EINVAL, "a request takes 1 to 4 inputs");
+  for (int k = 0; k < nin; ++k) {
+    if (!ins[k]) throw GError(GPUOS_EINVAL, std::string(names[k]) + " is required");
+    check_tensor(*ins[k], names[k]);
+  }
+  check_tensor(out, "output");
+  const int nd = out.ndim;
+  int64_t st[4][kMaxDims] = {};
+  for (int k = 0; k < nin; ++k) broadcast_to(*ins[k], out, st[k], names[k]);
+  const int64_t numel = numel_of(out);
+
+  struct Dim { int64_t n, s[4], o; };
+  Dim dims[kMaxDims];
+  int kd = 0;
+  for (int d = 0; d < nd; ++d)
+    if (out.sizes[d] != 1) {
+      Dim x{out.sizes[d], {0, 0, 0, 0}, out.strides[d]};
+      for (int k = 0; k < nin; ++k) x.s[k] = st[k][d];
+      dims[kd++] = x;
+    }
+  Dim cd[kMaxDims];
+  int m = 0;
+  for (int i = 0; i < kd; ++i) {
+    const Dim& x = dims[i];
+    bool merge = m > 0 && cd[m - 1].o == x.o * x.n;
+    for (int k = 0; k < nin && merge; ++k) merge = cd[m - 1].s[k] == x.s[k] * x.n;
+    if (merge) {
+      Dim y = x;
+      y.n = cd[m - 1].n * x.n;
+      cd[m - 1] = y;
+    } else {
+      cd[m++] = x;
+    }
+  }
+
+  Req& q = p.r;
+  std::memset(&q, 0, sizeof(q));
+  q.op = (uint16_t)op;
+  q.kind = RK_EW;
+  q.dta = (uint8_t)ins[0]->dtype;
+  q.dtb = (uint8_t)ins[1]->dtype;
+  q.dto = (uint8_t)out.dtype;
+  q.flags = (uint8_t)(RF_HAS_B | RF_NARY | (is_slot ? RF_SLOT : 0));
+  q.p0 = p0;
+  q.p1 = p1;
+  q.numel = numel;
+  q.a = reinterpret_cast<uint64_t>(ins[0]->data);
+  q.b = reinterpret_cast<uint64_t>(ins[1]->data);
+  q.o = reinterpret_cast<uint64_t>(out.data);
+  p.has_ext = true;
+  std::memset(&p.ext, 0, sizeof(p.ext));
+  p.ext.c = reinterpret_cast<uint64_t>(ins[2]->data);
+  p.ext.dtc = ins[2]->dtype;
+  p.ext.d = nin > 3 ? reinterpret_cast<uint64_t>(ins[3]->data) : 0;
+  p.ext.dtd = nin > 3 ? ins[3]->dtype : ins[2]->dtype;
+
+  bool unit = m <= 1 && (m == 0 || cd[0].o == 1);
+  for (int k = 0; k < nin && unit && m == 1; ++k) unit = cd[0].s[k] == 0 || cd[0].s[k] == 1;
+  if (unit) {
+    q.layout = EL_CONTIG;
+    if (m == 0 || cd[0].s[0] == 0) q.flags |= RF_A_SCALAR;
+    if (m == 0 || cd[0].s[1] == 0) q.flags |= RF_B_SCALAR;
+    p.ext.sc[0] = m ? cd[0].s[2] : 0;
+    p.ext.sd[0] = (m && nin > 3) ? cd[0].s[3] : 0;
+  } else if (m <= 2 && cd[m - 1].o == 1) {
+    const int64_t N = cd[m - 1].n;
+    q.layout = EL_ROW2D;
+    q.inner = N;
+    q.sa_row = m == 2 ? cd[0].s[0] : 0;
+    q.sb_row = m == 2 ? cd[0].s[1] : 0;
+    q.so_row = m == 2 ? cd[0].o : 0;
+    q.sa_in = cd[m - 1].s[0];
+    q.sb_in = cd[m - 1].s[1];
+    p.ext.sc[0] = m == 2 ? cd[0].s[2] : 0;
+    p.ext.sc[1] = cd[m - 1].s[2];
+    p.ext.sd[0] = (m == 2 && nin > 3) ? cd[0].s[3] : 0;
+    p.ext.sd[1] = nin > 3 ? cd[m - 1].s[3] : 0;
+    if (numel >= (1ll << 31) || N >= (1ll << 31)) {
+      q.flags |= RF_BIG;
+    } else {
+      uint32_t sh = 0;
+      q.fdiv_m = fdiv_magic((uint32_t)N, &sh);
+      q.fdiv_s = sh;
+    }
+  } else {
+    q.layout = EL_STRIDED;
+    p.ext.ndim = m;
+    for (int i = 0; i < m; ++i) {
+      p.ext.sizes[i] = cd[i].n;
+      p.ext.sa[i] = cd[i].s[0];
+      p.ext.sb[i] = cd[i].s[1];
+      p.ext.sc[i] = cd[i].s[2];
+      p.ext.sd[i] = nin > 3 ? cd[i].s[3] : 0;
+      p.ext.so[i] = cd[i].o;
+    }
+  }
+  const uint32_t ce = 2048u;
+  q.chunk = ce;
+  p.nchunk = (uint32_t)((numel + ce - 1) / ce);
+  p.out_ext = extent_of(out);
+  for (int k = 0; k < nin; ++k) p.in_ext[k] = extent_of(*ins[k]);
+  p.nin = nin;
+}
+
 void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
                             const gpuos_tensor& out, const int32_t* axes, int naxes,
                             bool keepdim) {
@@ -652,7 +763,8 @@ void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
   q.o = reinterpret_cast<uint64_t>(out.data);
   q.nseg = 1;
   const int e = esz(x.dtype);
-  constexpr int64_t kSeg = 8192;
+  // elements per chunk (or per segment of a long row): 32 KB of input
+  const int64_t kSeg = 32768 / e;
 
   if (mk <= 1 && mr <= 1) {
     const int64_t sr = mk ? ck[0].sa : 0, so = mk ? ck[0].so : 0;
@@ -662,9 +774,13 @@ void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
     q.sa_in = sc;
     if (sc == 1) {
       q.layout = RL_ROWS;
-      if ((q.a & 15) == 0 && (R == 1 || ((sr * e) & 15) == 0)) q.flags |= RF_VEC;
+      // rows are read in aligned 16-byte blocks, whatever their alignment
+      q.flags |= RF_VEC;
       if (C <= kSeg) {
-        const uint32_t G = std::min<uint32_t>(32, pow2_ceil((uint64_t)std::max<int64_t>(1, (C + 15) / 16)));
+        // lanes per row: as many as leave each lane at most 8 of the 16-byte
+        // blocks a row touches, so that a row step is one round of loads
+        const uint64_t nbl = (uint64_t)(C * e + 15) / 16 + 1;
+        const uint32_t G = std::min<uint32_t>(32, pow2_ceil((nbl + 7) / 8));
         const uint32_t per = 32 / G;
         uint64_t rpc = (uint64_t)std::max<int64_t>(1, kSeg / std::max<int64_t>(C, 1));
         rpc = std::max<uint64_t>(per, rpc / per * per);
@@ -768,6 +884,28 @@ void Executor::submit_ew(int op, bool is_slot, float p0, float p1, const gpuos_t
   }
   ++requests_;
   if (pending_.back().nchunk == 0) pending_.pop_back();  // empty output: nothing to do
+}
+
+void Executor::submit_nary(int slot, const gpuos_tensor* const* ins, int nin,
+                           const gpuos_tensor& out) {
+  std::lock_guard<std::mutex> lk(mu_);
+  if (!started_) throw GError(GPUOS_ESTATE, "executor is shut down");
+  if (slot < 0 || slot >= kMaxSlots) throw GError(GPUOS_EINVAL, "slot out of range");
+  const int phys = tab_.alias[slot];
+  const SlotEntry& e = tab_.slot[phys >= 0 && phys < kMaxSlots ? phys : slot];
+  if (e.arity != nin)
+    throw GError(GPUOS_EINVAL, "slot " + std::to_string(slot) + " takes " +
+                                   std::to_string(e.arity) + " inputs, got " +
+                                   std::to_string(nin));
+  pending_.emplace_back();
+  try {
+    build_ew_nary(pending_.back(), slot, true, 0.f, 0.f, ins, nin, out);
+  } catch (...) {
+    pending_.pop_back();
+    throw;
+  }
+  ++requests_;
+  if (pending_.back().nchunk == 0) pending_.pop_back();
 }
 
 void Executor::submit_reduce(int op, bool is_slot, const gpuos_tensor& x,
@@ -1002,22 +1140,31 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       after_prev = lz;
     }
   }
-  // Time per element of a request's chunks relative to a light operator's
-  // fp32 vector chunk: the operator's weight, times 2 for the vector body
-  // with per-row operands and 4 for the general body (from per-chunk timings).
-  auto ew_cost = [](const Pending& p, int v) -> uint64_t {
-    uint64_t w = (uint64_t)chunk_weight(v);
+  // Time per element of a request's chunks, in units of half a light
+  // operator's fp32 vector element: the operator's weight, times 2 for the
+  // vector body with per-row operands and 4 for the general body (from
+  // per-chunk timings); a vector request whose operands and output are all
+  // 16-bit moves half the bytes per element and counts half.
+  auto ew_cost = [](const Pending& p, int v, bool* halved) -> uint64_t {
+    uint64_t w = 2 * (uint64_t)chunk_weight(v);
+    const bool vec = (p.r.flags & RF_VEC) && p.r.layout != EL_STRIDED;
     if (p.r.layout == EL_TILE2D) w *= 2;
-    else if (!(p.r.flags & RF_VEC) || p.r.layout == EL_STRIDED) w *= 4;
+    else if (!vec) w *= 4;
     else if (p.r.layout == EL_ROW2D) w *= 2;
+    const bool narrow = p.r.dto != kF32 && ((p.r.flags & RF_A_SCALAR) || p.r.dta != kF32) &&
+                        (!(p.r.flags & RF_HAS_B) || (p.r.flags & RF_B_SCALAR) || p.r.dtb != kF32);
+    *halved = vec && narrow;
+    if (*halved) w /= 2;
     return w;
   };
   // Elementwise chunk size for this batch: about two light-operator chunks'
-  // worth of work per resident warp (multiple of 512 elements, 512..8192),
+  // worth of work per resident warp, as a multiple of 512 elements in
+  // 512..8192 of a light fp32 operator,
   // counting each element at its cost; a request's chunks get 1/cost of that
   // (at least 128 elements).
   std::vector<int> var(n);
   std::vector<uint8_t> cost_log2(n);  // every cost is a power of two
+  std::vector<uint8_t> narrow(n, 0);  // 1: the cost counted half for 16-bit data
   uint64_t ew_work = 0;
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + r];
@@ -1029,8 +1176,10 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     }
     var[r] = v;
     if (p.r.kind == RK_EW) {
-      const uint64_t w = ew_cost(p, v);
+      bool halved = false;
+      const uint64_t w = ew_cost(p, v, &halved);
       cost_log2[r] = (uint8_t)__builtin_ctzll(w);
+      narrow[r] = halved ? 1 : 0;
       ew_work += (uint64_t)p.r.numel << cost_log2[r];
     }
   }
@@ -1044,8 +1193,8 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   }
   const uint64_t warps = lean ? (uint64_t)std::max(1, lean_warps_)
                               : (uint64_t)std::max(1, total_warps_);
-  uint64_t ce = align_up(std::max<uint64_t>(1, ew_work / (2 * warps)), 512);
-  ce = std::min<uint64_t>(std::max<uint64_t>(ce, 512), 8192);
+  uint64_t ce = align_up(std::max<uint64_t>(1, ew_work / (2 * warps)), 1024);
+  ce = std::min<uint64_t>(std::max<uint64_t>(ce, 1024), 16384);
   // A batch with stage barriers runs its stages one after another, each on
   // as many warps as it has chunks: a stage's chunks are sized from its own
   // work spread over every warp (one chunk per granule, below), not from the
@@ -1057,20 +1206,25 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       if (reqs[i + r].r.kind == RK_EW) sw[stage_first[r]] += (uint64_t)reqs[i + r].r.numel << cost_log2[r];
     stage_ce.resize(n);
     for (uint32_t r = 0; r < n; ++r) {
-      const uint64_t c = align_up(std::max<uint64_t>(1, sw[stage_first[r]] / warps), 128);
-      stage_ce[r] = std::min<uint64_t>(std::max<uint64_t>(c, 512), 8192);
+      const uint64_t c = align_up(std::max<uint64_t>(1, sw[stage_first[r]] / warps), 256);
+      stage_ce[r] = std::min<uint64_t>(std::max<uint64_t>(c, 1024), 16384);
     }
   }
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + r];
     if (p.r.kind != RK_EW) continue;
-    uint64_t c = std::max<uint64_t>(128, (staged ? stage_ce[r] : ce) >> cost_log2[r]);
+    // (a batch with stage barriers is latency-bound: its chunks are sized in
+    // elements, the 16-bit discount left out, so that a stage spreads over
+    // as many warps as before)
+    uint64_t c = std::max<uint64_t>(
+        128, staged ? stage_ce[r] >> (cost_log2[r] + narrow[r]) : ce >> cost_log2[r]);
     if (p.r.layout == EL_TILE2D) {
-      // whole columns: c elements make c / rows columns, a multiple of 32
+      // whole columns: c elements make c / rows columns, a multiple of the
+      // 32 x kTileC columns a warp covers per pass (64)
       const uint64_t R = std::max<uint32_t>(1u, p.r.nseg), N = (uint64_t)p.r.inner;
-      uint64_t cols = align_up(std::max<uint64_t>(1, c / R), 32);
+      uint64_t cols = align_up(std::max<uint64_t>(1, c / R), 64);
       const uint64_t k = (N + cols - 1) / cols;
-      cols = align_up((N + k - 1) / k, 32);
+      cols = align_up((N + k - 1) / k, 64);
       p.r.chunk = (uint32_t)cols;
       p.nchunk = (uint32_t)((N + cols - 1) / cols);
       continue;
@@ -1135,6 +1289,11 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   const uint64_t warps_all = (uint64_t)std::max(1, total_warps_);
   uint64_t gran = staged ? 1 : nchunk / (8 * warps_all);
   gran = std::min<uint64_t>(std::max<uint64_t>(gran, 1), 8);
+  // A batch of at least 16 chunks per warp (the large reductions) has its
+  // warps claim granules one at a time, so that chunks of different costs
+  // (dtypes, layouts) even out across warps; at that size the claims (one
+  // atomic per granule of up to 8 chunks) are noise.
+  const bool claim = !staged && nchunk >= 16 * warps_all;
   const uint64_t ngran = (nchunk + gran - 1) / gran;
   const uint64_t rec_off = sizeof(BatchHdr);
   const uint64_t cb_off = rec_off + 128ull * n;
@@ -1160,7 +1319,8 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   h->rec_off = (uint32_t)rec_off;
   h->cb_off = (uint32_t)cb_off;
   h->bytes = (uint32_t)bytes;
-  h->flags = (staged ? BF_STAGED : 0u) | (after_prev ? BF_AFTER_PREV : 0u);
+  h->flags = (staged ? BF_STAGED : 0u) | (after_prev ? BF_AFTER_PREV : 0u) |
+             (claim ? BF_CLAIM : 0u);
   h->scratch = floats ? reinterpret_cast<uint64_t>(partials_ + poff) : 0;
   h->counters = reinterpret_cast<uint64_t>(counters_);
   h->wait_from = done_wm_;
@@ -1729,9 +1889,9 @@ int Executor::register_elementwise(const std::string& key, const std::string& ex
   std::lock_guard<std::mutex> lk(mu_);
   auto it = slot_of_key_.find(key);
   if (it != slot_of_key_.end()) return it->second;
-  if (arity != 1 && arity != 2) throw GError(GPUOS_EINVAL, "arity must be 1 or 2");
+  if (arity < 1 || arity > 4) throw GError(GPUOS_EINVAL, "arity must be 1 to 4");
   float p0 = 0.f, p1 = 0.f;
-  int v = match_builtin_expr(expr, arity, &p0, &p1);
+  int v = arity <= 2 ? match_builtin_expr(expr, arity, &p0, &p1) : -1;
   if (next_slot_ >= kMaxSlots) throw GError(GPUOS_EINVAL, "jump table is full (128 slots)");
   if (v < 0) {
     // not a precompiled operator: compile it (with the earlier custom ones)
@@ -2085,6 +2245,19 @@ int32_t gpuos_submit_binary(gpuos_executor* ex, int32_t slot, const gpuos_tensor
   });
 }
 
+int32_t gpuos_submit_nary(gpuos_executor* ex, int32_t slot, int32_t nin,
+                          const gpuos_tensor* ins, const gpuos_tensor* out) {
+  return guard([&] {
+    if (!ins || !out) throw GError(GPUOS_EINVAL, "inputs and out are required");
+    if (nin < 1 || nin > 4) throw GError(GPUOS_EINVAL, "a request takes 1 to 4 inputs");
+    if (nin <= 2) {
+      X(ex)->submit_ew(slot, true, 0.f, 0.f, &ins[0], nin == 2 ? &ins[1] : nullptr, *out);
+      return;
+    }
+    const gpuos_tensor* p[4] = {&ins[0], &ins[1], &ins[2], nin > 3 ? &ins[3] : nullptr};
+    X(ex)->submit_nary(slot, p, nin, *out);
+  });
+}
 int32_t gpuos_register_elementwise(gpuos_executor* ex, const char* key, const char* expr,
                                    int32_t arity, int32_t* slot_out) {
   return guard([&] {

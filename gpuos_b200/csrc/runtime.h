@@ -91,7 +91,7 @@ struct Pending {
   bool has_ext = false;
   ExtRec ext;
   Extent out_ext;
-  Extent in_ext[2];
+  Extent in_ext[4];
   int nin = 0;
   uint32_t nchunk = 0;
   uint64_t partials = 0;  // floats of scratch this request needs
@@ -111,6 +111,7 @@ class Executor {
   // submission (thread-safe)
   void submit_ew(int op, bool is_slot, float p0, float p1, const gpuos_tensor* a,
                  const gpuos_tensor* b, const gpuos_tensor& out);
+  void submit_nary(int slot, const gpuos_tensor* const* ins, int nin, const gpuos_tensor& out);
   void submit_reduce(int op, bool is_slot, const gpuos_tensor& x, const gpuos_tensor& out,
                      const int32_t* axes, int naxes, bool keepdim);
   void submit_task(const void* task);
@@ -251,6 +252,8 @@ class Executor {
 // choice, vector-path legality and chunking of one request.
 void build_ew(Pending& p, int op, bool is_slot, float p0, float p1, const gpuos_tensor* a,
               const gpuos_tensor* b, const gpuos_tensor& out);
+void build_ew_nary(Pending& p, int op, bool is_slot, float p0, float p1,
+                   const gpuos_tensor* const* ins, int nin, const gpuos_tensor& out);
 void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
                   const gpuos_tensor& out, const int32_t* axes, int naxes, bool keepdim);
 

@@ -17,12 +17,25 @@ scheduler.py:19; read when the context is entered).
   scheduled, with the reference's expression strings (scheduler.py:145-153,
   192-205, 244-290) registered through ``register_elementwise``.
 
-Each scheduled op is submitted at once and writes the tensor it returns.  The
-reference instead defers binary and unary results into "fused" nodes that it
-later computes into a freshly allocated tensor, so the returned tensor never
-receives the result (scheduler.py:118, 157-160, 349-358).  Chains need no
-fusion for correctness here: the executor orders a request after the earlier
-requests of the flush whose outputs it reads.
+Every scheduled op writes the tensor it returns.  The reference defers
+binary and unary results into "fused" nodes that it later computes into a
+freshly allocated tensor, so the returned tensor never receives the result
+(scheduler.py:118, 157-160, 349-358), and it composes only a unary op on top
+of one node (scheduler.py:213-222).  Here, with the JIT switch on (and
+``GPUOS_SCHEDULER_FUSE`` not ``'0'``), an elementwise op whose input is the
+result of an earlier elementwise op that has not been submitted yet inlines
+that op's expression: ``torch.sigmoid(a * b) + c`` becomes one request,
+``(gpuos_keep_f32(1.f / (1.f + expf(-(gpuos_keep_f32((A * B))))))) + C``
+over the leaves a, b, c (up to four leaves: operands A..D of a custom
+expression).  Each inlined intermediate is rounded as the unfused chain
+would have stored it (``gpuos_keep_<dtype>``: its dtype's rounding, and for
+fp32 no contraction into the consuming operation), so a fused chain gives
+the unfused chain's values.  The ops are submitted when something needs
+them: a reduction or a torch op that reads their memory, a flush, the end of
+the context.  An intermediate whose tensor the caller no longer holds by then
+is not written at all; one that is still held is written as well.  Without
+fusion the executor still orders each request after the earlier requests of
+the flush whose outputs it reads.
 
 An op that is not scheduled and reads memory a pending request writes, or
 writes memory a pending request reads or writes, forces a synchronous flush
@@ -37,6 +50,8 @@ from __future__ import annotations
 
 import contextlib
 import os
+import re
+import sys
 import threading
 from typing import Any, Dict, List, Optional, Set, Tuple
 
@@ -46,6 +61,33 @@ from . import load as _load
 
 def _jit_disabled() -> bool:
     return os.environ.get("GPUOS_SCHEDULER_DISABLE_JIT", "1") not in ("0", "false", "False")
+
+
+def _fuse_enabled() -> bool:
+    return os.environ.get("GPUOS_SCHEDULER_FUSE", "1") not in ("0", "false", "False")
+
+
+_LETTERS = "ABCD"
+_TOKEN = re.compile(r"\b([A-D])\b")
+_KEEP = {torch.float32: "gpuos_keep_f32", torch.float16: "gpuos_keep_f16",
+         torch.bfloat16: "gpuos_keep_bf16"}
+_MAX_EXPR = 4000  # characters: an operand used twice doubles the text
+
+
+def _rename(expr: str, mapping: Dict[str, str]) -> str:
+    """Rename the operand letters of `expr` in one pass."""
+    return _TOKEN.sub(lambda m: mapping.get(m.group(1), m.group(1)), expr)
+
+
+class _Node:
+    """An elementwise op not yet submitted: `expr` over the operand letters
+    A.. (one per leaf tensor), writing `out`."""
+    __slots__ = ("expr", "leaves", "out")
+
+    def __init__(self, expr: str, leaves: List[torch.Tensor], out: torch.Tensor):
+        self.expr = expr
+        self.leaves = leaves
+        self.out = out
 
 _BINARY_BUILTIN = {
     "aten::add.Tensor": "submit_add",
@@ -156,9 +198,13 @@ def _add(e, table):
 
 class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
     def __init__(self, ext, *, size_threshold: int, auto_flush_ms: Optional[float],
-                 pending: Set[int], jit: bool):
+                 pending: Set[int], jit: bool, fuse: bool = False):
         super().__init__()
         self.ext = ext
+        self.fuse = jit and fuse
+        # elementwise ops not yet submitted, by id of the tensor they return,
+        # in the order they were made (with their slots)
+        self._nodes: Dict[int, Tuple[_Node, int]] = {}
         self.size_threshold = size_threshold
         self.auto_flush_ms = auto_flush_ms
         self.pending = pending  # data_ptr of every output not yet flushed synchronously
@@ -230,6 +276,96 @@ class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
             _add(_extent(t), self._r)
         return out
 
+    # ---- fused chains --------------------------------------------------------
+    def _operand(self, t: torch.Tensor, expand: bool):
+        """(expression, leaves) standing for tensor `t`: the expression of the
+        unsubmitted op that returned it, rounded as its dtype stores it, or
+        the tensor itself."""
+        if expand:
+            e = self._nodes.get(id(t))
+            if e is not None and e[0].out is t and t.dtype in _KEEP:
+                return f"{_KEEP[t.dtype]}({e[0].expr})", e[0].leaves
+        return "A", [t]
+
+    @staticmethod
+    def _compose(expr: str, operands) -> Optional[Tuple[str, List[torch.Tensor]]]:
+        """Substitute the operand letters of an op's expression (A, B) by the
+        operands' expressions, merging their leaves (at most four)."""
+        leaves: List[torch.Tensor] = []
+        mapping: Dict[str, str] = {}
+        for letter, (sub, sl) in zip("AB", operands):
+            ren: Dict[str, str] = {}
+            for k, t in enumerate(sl):
+                idx = next((j for j, u in enumerate(leaves) if u is t), None)
+                if idx is None:
+                    leaves.append(t)
+                    idx = len(leaves) - 1
+                if idx >= len(_LETTERS):
+                    return None
+                ren[_LETTERS[k]] = _LETTERS[idx]
+            mapping[letter] = "(" + _rename(sub, ren) + ")" if sub != "A" else ren["A"]
+        out = _TOKEN.sub(lambda m: mapping.get(m.group(1), m.group(1)), expr)
+        if len(out) > _MAX_EXPR:
+            return None
+        return out, leaves
+
+    def _node(self, key: str, expr: str, inputs: List[torch.Tensor], out: torch.Tensor):
+        """Defer the elementwise op `expr` over `inputs` writing `out`,
+        inlining the unsubmitted ops its inputs come from where the operands
+        (at most four leaves) and the JIT allow."""
+        ext = self.ext
+        tries = [(True,) * len(inputs)]
+        if len(inputs) == 2:
+            tries += [(True, False), (False, True)]
+        def deferred(t):
+            e = self._nodes.get(id(t))
+            return e is not None and e[0].out is t and t.dtype in _KEEP
+
+        for expand in tries:
+            if not any(x and deferred(t) for t, x in zip(inputs, expand)):
+                continue  # nothing to inline
+            c = self._compose(expr, [self._operand(t, x) for t, x in zip(inputs, expand)])
+            if c is None:
+                continue
+            cexpr, leaves = c
+            try:
+                slot = ext.register_elementwise(f"fused|{len(leaves)}|{cexpr}", cexpr, len(leaves))
+            except Exception:  # NVRTC missing or out of custom slots: do not inline
+                continue
+            self._nodes[id(out)] = (_Node(cexpr, leaves, out), slot)
+            return self._done(out, *leaves)
+        slot = ext.register_elementwise(key, expr, len(inputs))
+        self._nodes[id(out)] = (_Node(expr, list(inputs), out), slot)
+        return self._done(out, *inputs)
+
+    def submit_nodes(self):
+        """Submit the deferred ops in the order they were made.  An op whose
+        returned tensor nobody else holds any more (only this node refers to
+        it) was inlined into the ops that read it, or is unused: it is not
+        written."""
+        if not self._nodes:
+            return
+        nodes = list(self._nodes.values())
+        self._nodes.clear()
+        ext = self.ext
+        for node, slot in nodes:
+            # references: node.out, and getrefcount's own argument
+            if sys.getrefcount(node.out) <= 2:
+                continue
+            lv = node.leaves
+            if len(lv) == 1:
+                ext.submit_unary(slot, lv[0], node.out)
+            elif len(lv) == 2:
+                ext.submit_binary(slot, lv[0], lv[1], node.out)
+            else:
+                ext.submit_nary(slot, lv, node.out)
+        del nodes
+
+    def sync(self):
+        self.submit_nodes()
+        self.ext.flush(sync=True)
+        self.clear_pending()
+
     def clear_pending(self):
         self.pending.clear()
         self.pending_in.clear()
@@ -255,8 +391,7 @@ class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
         # runs in torch: pending requests it depends on must be done first
         if self.pending and (self._reads_pending(args, kwargs) or
                              self._writes_pending(func, args, kwargs)):
-            self.ext.flush(sync=True)
-            self.clear_pending()
+            self.sync()
         return func(*args, **kwargs)
 
     def _schedule(self, name, func, args, kwargs):
@@ -279,6 +414,8 @@ class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
                 return None
             if not self.jit:
                 getattr(ext, _BINARY_BUILTIN[name])(a, b, out)
+            elif self.fuse:
+                return self._node(f"bin|{name}", _BINARY_EXPR[name], [a, b], out)
             else:
                 slot = ext.register_elementwise(f"bin|{name}", _BINARY_EXPR[name], 2)
                 ext.submit_binary(slot, a, b, out)
@@ -299,6 +436,8 @@ class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
             out = self._out_for(kwargs, x.shape, x.dtype, x.device)
             if out is None:
                 return None
+            if self.fuse:
+                return self._node(key, expr, [x], out)
             slot = ext.register_elementwise(key, expr, 1)
             ext.submit_unary(slot, x, out)
             return self._done(out, x)
@@ -321,6 +460,7 @@ class _GPUOSSchedulerMode(torch.utils._python_dispatch.TorchDispatchMode):
                 [s for i, s in enumerate(x.shape) if i not in axes]
             out = torch.empty(shape, dtype=x.dtype, device=x.device)
             op = _REDUCE[name]
+            self.submit_nodes()  # its input may be a deferred op's result
             slot = ext.register_reduce(f"reduce_{op}", op)
             ext.submit_reduce(slot, x, out, axes, keepdim)
             return self._done(out, x)
@@ -345,11 +485,14 @@ class GPUOSScheduler:
         self.ext.init(self.capacity, self.threads_per_block)
         self._mode = _GPUOSSchedulerMode(self.ext, size_threshold=self.size_threshold,
                                          auto_flush_ms=self.auto_flush_ms,
-                                         pending=self._pending, jit=not _jit_disabled())
+                                         pending=self._pending, jit=not _jit_disabled(),
+                                         fuse=_fuse_enabled())
         self._mode.__enter__()
         return self
 
     def flush(self, sync: bool = False):
+        if self._mode is not None:
+            self._mode.submit_nodes()
         self.ext.flush(sync=sync)
         if sync:
             self._pending.clear()
@@ -360,6 +503,7 @@ class GPUOSScheduler:
         try:
             if self._mode is not None:
                 self._mode.close()
+                self._mode.submit_nodes()
                 self._mode.__exit__(exc_type, exc, tb)
         finally:
             self._mode = None

@@ -127,10 +127,22 @@ int32_t gpuos_submit_unary(gpuos_executor* ex, int32_t slot, const gpuos_tensor*
 int32_t gpuos_submit_binary(gpuos_executor* ex, int32_t slot, const gpuos_tensor* a,
                             const gpuos_tensor* b, const gpuos_tensor* out);
 
+/* Queue a request of `nin` (1 to 4) inputs ins[0..nin-1] through slot `slot`:
+ * out = expr(A, B, C, D).  No counterpart in the reference, whose requests
+ * carry at most two inputs (src/common.h:34-46); it lets a chain of
+ * elementwise ops composed into one expression (a fused chain of the
+ * scheduler) run as one request.  The slot's arity must equal nin. */
+int32_t gpuos_submit_nary(gpuos_executor* ex, int32_t slot, int32_t nin,
+                          const gpuos_tensor* ins, const gpuos_tensor* out);
+
 /* Register an fp32 expression over A (and B) and return its slot (replaces
  * register_elementwise: gpuos_ext.cpp:681-692).  The expressions the
  * reference scheduler emits map onto precompiled operators; any other
- * expression is compiled with NVRTC for sm_100a. */
+ * expression is compiled with NVRTC for sm_100a.  Arity 3 and 4 (operands C
+ * and D, for gpuos_submit_nary) go beyond the reference's 1 and 2.  Custom
+ * expressions may call gpuos_keep_f32 / gpuos_keep_f16 / gpuos_keep_bf16(x):
+ * the value x has once stored in that dtype, with the rounding of a separate
+ * operation (no contraction into the operation that consumes it). */
 int32_t gpuos_register_elementwise(gpuos_executor* ex, const char* key, const char* expr,
                                    int32_t arity, int32_t* slot_out);
 

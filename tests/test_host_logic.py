@@ -138,7 +138,7 @@ def test_plan_reductions():
     assert p["nchunk"] == 47 and p["partials"] == 47 * 128 and p["counters"] == 1
     xb = torch.randn(3000, 256, dtype=torch.bfloat16).t()    # bf16: 8 rows per lane
     p = C.plan_reduce(C.variant("sum"), xb, torch.empty(256, dtype=torch.bfloat16), [1], False)
-    assert p["flags"] & 2 and p["rg"] == 256 and p["chunk"] == 32
+    assert p["flags"] & 2 and p["rg"] == 256 and p["chunk"] == 64   # 32 KB chunks
     xo = torch.randn(3000, 99).t()                              # 99 rows: not a multiple of 4
     p = C.plan_reduce(C.variant("mean"), xo, torch.empty(99), [1], False)
     assert (p["layout"], p["rg"]) == (1, 32) and not p["flags"] & 2
