@@ -93,6 +93,26 @@ SIGNATURES = {
                                                 P(ctypes.c_int32), P(ctypes.c_float),
                                                 P(ctypes.c_float)]),
     "gpuos_get_stats": (ctypes.c_int32, [_VP, P(Stats)]),
+    "gpuos_ipc_server_create": (ctypes.c_int32, [ctypes.c_char_p, ctypes.c_int32, ctypes.c_uint64,
+                                                 ctypes.c_int32, ctypes.c_int32, P(Options),
+                                                 P(_VP)]),
+    "gpuos_ipc_server_destroy": (ctypes.c_int32, [_VP]),
+    "gpuos_ipc_server_stats": (ctypes.c_int32, [_VP, P(ctypes.c_uint64), P(ctypes.c_uint64),
+                                                P(ctypes.c_uint64), P(ctypes.c_int32)]),
+    "gpuos_ipc_connect": (ctypes.c_int32, [ctypes.c_char_p, ctypes.c_double, P(_VP)]),
+    "gpuos_ipc_disconnect": (ctypes.c_int32, [_VP]),
+    "gpuos_ipc_pool": (ctypes.c_int32, [_VP, P(_VP), P(ctypes.c_uint64), P(ctypes.c_uint64),
+                                        P(ctypes.c_uint64), P(ctypes.c_int32)]),
+    "gpuos_ipc_submit_builtin": (ctypes.c_int32, [_VP, ctypes.c_int32, P(Tensor), P(Tensor),
+                                                  P(Tensor)]),
+    "gpuos_ipc_submit_slot": (ctypes.c_int32, [_VP, ctypes.c_int32, ctypes.c_int32, P(Tensor),
+                                               P(Tensor)]),
+    "gpuos_ipc_submit_reduce": (ctypes.c_int32, [_VP, ctypes.c_int32, P(Tensor), P(Tensor),
+                                                 P(ctypes.c_int32), ctypes.c_int32,
+                                                 ctypes.c_int32]),
+    "gpuos_ipc_flush": (ctypes.c_int32, [_VP, ctypes.c_int32]),
+    "gpuos_ipc_register": (ctypes.c_int32, [_VP, ctypes.c_int32, ctypes.c_char_p, ctypes.c_char_p,
+                                            ctypes.c_int32, P(ctypes.c_int32)]),
 }
 
 _lib = None

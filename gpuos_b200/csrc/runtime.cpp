@@ -1143,18 +1143,14 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   // Time per element of a request's chunks, in units of half a light
   // operator's fp32 vector element: the operator's weight, times 2 for the
   // vector body with per-row operands and 4 for the general body (from
-  // per-chunk timings); a vector request whose operands and output are all
-  // 16-bit moves half the bytes per element and counts half.
-  auto ew_cost = [](const Pending& p, int v, bool* halved) -> uint64_t {
+  // per-chunk timings).  (Counting 16-bit vector elements at half measured
+  // slower on the broadcast stream: their chunks are not cheaper per element.)
+  auto ew_cost = [](const Pending& p, int v) -> uint64_t {
     uint64_t w = 2 * (uint64_t)chunk_weight(v);
     const bool vec = (p.r.flags & RF_VEC) && p.r.layout != EL_STRIDED;
     if (p.r.layout == EL_TILE2D) w *= 2;
     else if (!vec) w *= 4;
     else if (p.r.layout == EL_ROW2D) w *= 2;
-    const bool narrow = p.r.dto != kF32 && ((p.r.flags & RF_A_SCALAR) || p.r.dta != kF32) &&
-                        (!(p.r.flags & RF_HAS_B) || (p.r.flags & RF_B_SCALAR) || p.r.dtb != kF32);
-    *halved = vec && narrow;
-    if (*halved) w /= 2;
     return w;
   };
   // Elementwise chunk size for this batch: about two light-operator chunks'
@@ -1164,7 +1160,6 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   // (at least 128 elements).
   std::vector<int> var(n);
   std::vector<uint8_t> cost_log2(n);  // every cost is a power of two
-  std::vector<uint8_t> narrow(n, 0);  // 1: the cost counted half for 16-bit data
   uint64_t ew_work = 0;
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + r];
@@ -1176,10 +1171,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     }
     var[r] = v;
     if (p.r.kind == RK_EW) {
-      bool halved = false;
-      const uint64_t w = ew_cost(p, v, &halved);
-      cost_log2[r] = (uint8_t)__builtin_ctzll(w);
-      narrow[r] = halved ? 1 : 0;
+      cost_log2[r] = (uint8_t)__builtin_ctzll(ew_cost(p, v));
       ew_work += (uint64_t)p.r.numel << cost_log2[r];
     }
   }
@@ -1213,11 +1205,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + r];
     if (p.r.kind != RK_EW) continue;
-    // (a batch with stage barriers is latency-bound: its chunks are sized in
-    // elements, the 16-bit discount left out, so that a stage spreads over
-    // as many warps as before)
-    uint64_t c = std::max<uint64_t>(
-        128, staged ? stage_ce[r] >> (cost_log2[r] + narrow[r]) : ce >> cost_log2[r]);
+    uint64_t c = std::max<uint64_t>(128, (staged ? stage_ce[r] : ce) >> cost_log2[r]);
     if (p.r.layout == EL_TILE2D) {
       // whole columns: c elements make c / rows columns, a multiple of the
       // 32 x kTileC columns a warp covers per pass (64)
@@ -1775,6 +1763,30 @@ uint64_t Executor::flush(bool sync, cudaStream_t stream) {
   return ticket;
 }
 
+// With mu_ held and every batch before `ticket` done: raise the error of a
+// failed batch among them (once).
+void Executor::raise_batch_error_locked(uint64_t ticket) {
+  if (err_seq_ != UINT64_MAX && err_seq_ < ticket) {
+    const uint32_t e = err_bits_;
+    err_seq_ = UINT64_MAX;
+    err_bits_ = 0;
+    std::string why;
+    if (e & ERR_BAD_OP) why += " a request used a slot with no registered operator;";
+    if (e & ERR_BAD_KIND) why += " a slot's operator does not fit the request kind;";
+    if (e & ERR_STAGE_TIMEOUT) why += " a stage barrier wait timed out;";
+    if (e & ERR_CUDA) why += " CUDA reported: " + cuda_err_ + ";";
+    throw GError(GPUOS_EDEVICE, "gpuos batch error:" + why);
+  }
+}
+
+bool Executor::poll(uint64_t ticket) {
+  std::lock_guard<std::mutex> lk(mu_);
+  reclaim();
+  if (done_wm_ < ticket) return false;
+  raise_batch_error_locked(ticket);
+  return true;
+}
+
 void Executor::wait(uint64_t ticket, double timeout_s) {
   if (timeout_s <= 0) timeout_s = sync_timeout_s_;
   const auto t0 = std::chrono::steady_clock::now();
@@ -1783,17 +1795,7 @@ void Executor::wait(uint64_t ticket, double timeout_s) {
       std::lock_guard<std::mutex> lk(mu_);
       reclaim();
       if (done_wm_ >= ticket) {
-        if (err_seq_ != UINT64_MAX && err_seq_ < ticket) {
-          const uint32_t e = err_bits_;
-          err_seq_ = UINT64_MAX;
-          err_bits_ = 0;
-          std::string why;
-          if (e & ERR_BAD_OP) why += " a request used a slot with no registered operator;";
-          if (e & ERR_BAD_KIND) why += " a slot's operator does not fit the request kind;";
-          if (e & ERR_STAGE_TIMEOUT) why += " a stage barrier wait timed out;";
-          if (e & ERR_CUDA) why += " CUDA reported: " + cuda_err_ + ";";
-          throw GError(GPUOS_EDEVICE, "gpuos batch error:" + why);
-        }
+        raise_batch_error_locked(ticket);
         return;
       }
       if (opt_.mode == GPUOS_MODE_PERSISTENT) ensure_worker_locked();

@@ -118,6 +118,7 @@ class Executor {
 
   uint64_t flush(bool sync, cudaStream_t stream);
   void wait(uint64_t ticket, double timeout_s);
+  bool poll(uint64_t ticket);  // every batch before `ticket` done (raises a batch's error)
 
   // jump table
   int register_elementwise(const std::string& key, const std::string& expr, int arity);
@@ -148,6 +149,7 @@ class Executor {
                     uint32_t n, const std::vector<int>& var, const std::vector<uint32_t>& order,
                     uint64_t nchunk, cudaStream_t stream);
   uint32_t take_batch_err(uint64_t seq);
+  void raise_batch_error_locked(uint64_t ticket);
   void reclaim();
   void ensure_worker_locked();
   void launch_worker_locked(uint64_t start);

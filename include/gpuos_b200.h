@@ -246,6 +246,56 @@ int32_t gpuos_plan_elementwise(int32_t variant, float p0, float p1, const gpuos_
 int32_t gpuos_plan_reduce(int32_t variant, const gpuos_tensor* x, const gpuos_tensor* out,
                           const int32_t* axes, int32_t naxes, int32_t keepdim, gpuos_plan* plan);
 
+/* ---- multi-process sharing ------------------------------------------------
+ * No counterpart in the reference, which gives every process its own
+ * persistent kernel and executor (benchmarks/bench_mps.py:54-92).  One server
+ * per GPU owns an executor and a device pool exported with CUDA IPC; client
+ * processes place their tensors in the pool (each in its own region) and
+ * write requests into their own ring in POSIX shared memory "/<name>".  The
+ * server drains every ring into the one executor, so requests of different
+ * processes share batches.  A client waits on its own flushes only.  A client
+ * process must finish the GPU work that produced its inputs before it
+ * flushes (the Python client synchronizes its current stream), and it may
+ * read results after a synchronous flush returns.  device < 0 creates a
+ * server in record mode: no GPU, no pool, requests are counted and every
+ * flush completes at once (protocol tests without a GPU). */
+typedef struct gpuos_ipc_server gpuos_ipc_server;
+typedef struct gpuos_ipc_client gpuos_ipc_client;
+
+int32_t gpuos_ipc_server_create(const char* name, int32_t device, uint64_t pool_bytes,
+                                int32_t max_clients, int32_t ring_entries,
+                                const gpuos_options* opt, gpuos_ipc_server** out);
+/* Stops the server thread, drains and shuts down the executor, frees the pool
+ * and removes the shared memory name; clients still connected see their waits
+ * end with GPUOS_ESTATE and must not use their pool mappings any more. */
+int32_t gpuos_ipc_server_destroy(gpuos_ipc_server* s);
+int32_t gpuos_ipc_server_stats(gpuos_ipc_server* s, uint64_t* requests, uint64_t* client_flushes,
+                               uint64_t* launch_flushes, int32_t* clients);
+
+/* Take a free client slot of server `name`; map its pool on the server's
+ * device.  Waits of this client give up after timeout_s (0: 60 s). */
+int32_t gpuos_ipc_connect(const char* name, double timeout_s, gpuos_ipc_client** out);
+/* Flush, wait for this client's requests, release the slot and the mapping. */
+int32_t gpuos_ipc_disconnect(gpuos_ipc_client* c);
+/* The pool as this process sees it, this client's region of it, the device. */
+int32_t gpuos_ipc_pool(gpuos_ipc_client* c, void** base, uint64_t* bytes, uint64_t* region_off,
+                       uint64_t* region_bytes, int32_t* device);
+/* The submission calls of the executor, over tensors in the pool. */
+int32_t gpuos_ipc_submit_builtin(gpuos_ipc_client* c, int32_t op, const gpuos_tensor* a,
+                                 const gpuos_tensor* b, const gpuos_tensor* out);
+int32_t gpuos_ipc_submit_slot(gpuos_ipc_client* c, int32_t slot, int32_t nin,
+                              const gpuos_tensor* ins, const gpuos_tensor* out);
+int32_t gpuos_ipc_submit_reduce(gpuos_ipc_client* c, int32_t slot, const gpuos_tensor* x,
+                                const gpuos_tensor* out, const int32_t* axes, int32_t naxes,
+                                int32_t keepdim);
+/* Publish a flush marker; sync: wait for this client's requests before it and
+ * raise the first error the server met in them. */
+int32_t gpuos_ipc_flush(gpuos_ipc_client* c, int32_t sync);
+/* kind 1: register_elementwise(key, expr, arity); kind 2: register_reduce(key,
+ * op_name in expr), run by the server; the slot is the server executor's. */
+int32_t gpuos_ipc_register(gpuos_ipc_client* c, int32_t kind, const char* key, const char* expr,
+                           int32_t arity, int32_t* slot_out);
+
 /* Compile a custom expression with NVRTC only, to check it (no GPU needed):
  * GPUOS_OK, GPUOS_ENVRTC with the compiler log in gpuos_last_error(), or
  * GPUOS_EUNSUPPORTED when NVRTC is not installed (replaces the compile step of
