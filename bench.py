@@ -488,7 +488,7 @@ def cpu_baseline(stream, min_seconds=5.0):
                       f"({el:.1f} s wall, liboracle.so on {used} threads)"}
 
 
-def decode_chain(ext, dev, batches=(1, 8, 64), layers=32, steps=20, warmup=3):
+def decode_chain(ext, dev, batches=(1, 8, 64), layers=32, steps=20, warmup=3, fused=True):
     """The transformer-decode pointwise chain (bf16), through the public API.
 
     Per layer: residual add; x*x; mean(-1, keepdim); + 1e-6; pow(-0.5); * rstd
@@ -498,7 +498,9 @@ def decode_chain(ext, dev, batches=(1, 8, 64), layers=32, steps=20, warmup=3):
     `layers` layers and one flush(sync=True); inputs are N(0, 0.02).
     Reports requests/s, the host's submit time per request, and the time
     from the step's flush(sync=True) call to its return (planning, the batch
-    on the GPU in stage order, completion)."""
+    on the GPU in stage order, completion).  `fused` adds the same chain with
+    the pointwise tail and the gate composed into custom expressions of four
+    and two operands (five requests a layer)."""
     from gpuos_b200 import workloads as W
     bf = torch.bfloat16
     H, F = 4096, 11008
@@ -553,6 +555,45 @@ def decode_chain(ext, dev, batches=(1, 8, 64), layers=32, steps=20, warmup=3):
                         "host_submit_ns_per_request": round(sub_s / n * 1e9, 1),
                         "flush_sync_us_per_step": round(fl_s / steps * 1e6, 1),
                         "flush_sync_ns_per_request": round(fl_s / n * 1e9, 1)}
+        if fused:
+            # the same layers with the seven pointwise requests after the mean
+            # composed into two custom expressions (what the scheduler's chain
+            # fusion builds): five requests and four dependent stages a layer
+            ev = float(eps.float())
+            k_tail = ext.register_elementwise(
+                "decode|tail",
+                "gpuos_keep_bf16(gpuos_keep_bf16(A * gpuos_keep_bf16(powf(gpuos_keep_bf16("
+                f"B + {ev:.9e}f), -0.5f))) * C) + D", 4)
+            k_gate = ext.register_elementwise(
+                "decode|gate", "gpuos_keep_bf16(1.f / (1.f + expf(-A))) * B", 2)
+            xf = {}
+            sub_s, fl_s, wall_s = 0.0, 0.0, 0.0
+            for it in range(warmup + steps):
+                t0 = time.perf_counter()
+                x = x0
+                for li, l in enumerate(L):
+                    ext.submit_add(x, l["res"], l["h"])
+                    ext.submit_mul(l["h"], l["h"], l["sq"])
+                    ext.submit_reduce(s_mean, l["sq"], l["ms"], [1], True)
+                    o = l["hw"]  # the fused tail writes here (xo keeps the unfused result)
+                    ext.submit_nary(k_tail, [l["h"], l["ms"], l["w"], l["bias"]], o)
+                    ext.submit_binary(k_gate, l["u"], l["u2"], l["gt"])
+                    x = o
+                t1 = time.perf_counter()
+                ext.flush(sync=True)
+                t2 = time.perf_counter()
+                if it >= warmup:
+                    sub_s += t1 - t0
+                    fl_s += t2 - t1
+                    wall_s += t2 - t0
+            nf = 5 * layers * steps
+            last_u, last_f = L[-1]["xo"].float(), L[-1]["hw"].float()
+            rel = float(((last_u - last_f).abs() / (last_u.abs() + 1e-3)).max())
+            out[f"b{b}"]["fused"] = {
+                "requests_per_step": 5 * layers,
+                "flush_sync_us_per_step": round(fl_s / steps * 1e6, 1),
+                "host_submit_ns_per_request": round(sub_s / nf * 1e9, 1),
+                "max_rel_diff_vs_unfused": round(rel, 5)}
     return out
 
 

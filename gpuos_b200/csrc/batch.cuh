@@ -93,7 +93,7 @@ __device__ __forceinline__ void decode(Cur& cur, const Exec& ex, const Req* rec,
     }
   }
   cur.vec = q.kind == RK_EW && (q.flags & RF_VEC) && !(q.flags & RF_NARY) &&
-            q.layout != EL_STRIDED && ew_known(cur.v);
+            q.layout != EL_STRIDED && ew_vec_known(cur.v);
   if (cur.vec) {
     cur.u = vec_view(q);
   } else if ((q.kind == RK_EW && (q.layout == EL_STRIDED || (q.flags & RF_NARY))) ||

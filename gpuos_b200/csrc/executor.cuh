@@ -24,8 +24,18 @@ namespace gpuos {
 
 #define GPUOS_FULL 0xffffffffu
 
-// The elementwise variants this kernel can run (GPUOS_ALL_EW).
+// The elementwise variants this kernel can run (GPUOS_APPLY_EW): the
+// precompiled operators, and in the kernel linked with custom expressions
+// those as well.
 __device__ __forceinline__ bool ew_known(int v) {
+#ifdef GPUOS_JIT_LINK
+  if (v >= V_JIT_BASE && v < V_JIT_BASE + kJitOps) return true;
+#endif
+  return v >= 0 && v < V_NUM_EW;
+}
+
+// The variants with vector bodies in this kernel (GPUOS_ALL_EW).
+__device__ __forceinline__ bool ew_vec_known(int v) {
 #ifdef GPUOS_JIT_LINK
   return v >= V_JIT_BASE && v < V_JIT_BASE + kJitOps;
 #else
@@ -1192,10 +1202,6 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
     ew_generic(q, x, v, p0, p1, e0, e1, ex.lane);
     return;
   }
-#ifdef GPUOS_JIT_LINK
-  // the kernel for custom expressions runs elementwise batches only
-  if (ex.lane == 0) set_err(ex, ERR_BAD_KIND);
-#else
   if constexpr (!(BODIES & BODY_RED)) {
     if (ex.lane == 0) set_err(ex, ERR_BAD_KIND);
     return;
@@ -1212,7 +1218,6 @@ __device__ __forceinline__ void process_chunk(const Exec& ex, const ReqView& q, 
   }
   else if (q.rg == 1) red_generic_warp(ex, q, x, mean, k);
   else red_generic(ex, q, x, mean, k);
-#endif
 }
 
 // Called by the thread that counted the last chunk of the batch.  The

@@ -1,9 +1,11 @@
-// The batch kernel for custom expressions, built relocatable (-rdc): the
-// operators of slots V_JIT_BASE + 0..15 are the external device functions
-// gpuos_jit_op0..15, which the runtime compiles from the registered
+// The batch kernel for batches with custom expressions, built relocatable
+// (-rdc): the operators of slots V_JIT_BASE + 0..15 are the external device
+// functions gpuos_jit_op0..15, which the runtime compiles from the registered
 // expression strings with NVRTC and links to this code with the driver's
 // linker (runtime.cpp, JitOps).  Same batch format, chunking and completion
-// as gpuos_batch_kernel; elementwise requests only.
+// as gpuos_batch_kernel, and every body of it as well, so that a batch that
+// mixes custom expressions with precompiled operators and reductions runs in
+// one launch.
 #define GPUOS_JIT_LINK 1
 #include "batch.cuh"
 

@@ -82,25 +82,33 @@ __device__ __forceinline__ float op1(float A, float B, float p0, float p1) {
 }
 
 #define GPUOS_CASE1(V) case V: r = op1<V>(A, B, p0, p1); return true;
-// The elementwise variants a kernel instantiates: the precompiled operators,
-// or (in the kernel for custom expressions) the custom slots.
-#ifdef GPUOS_JIT_LINK
-#define GPUOS_ALL_EW(M) \
-  M(V_JIT_BASE + 0) M(V_JIT_BASE + 1) M(V_JIT_BASE + 2) M(V_JIT_BASE + 3) \
-  M(V_JIT_BASE + 4) M(V_JIT_BASE + 5) M(V_JIT_BASE + 6) M(V_JIT_BASE + 7) \
-  M(V_JIT_BASE + 8) M(V_JIT_BASE + 9) M(V_JIT_BASE + 10) M(V_JIT_BASE + 11) \
-  M(V_JIT_BASE + 12) M(V_JIT_BASE + 13) M(V_JIT_BASE + 14) M(V_JIT_BASE + 15)
-#else
-#define GPUOS_ALL_EW(M) \
+// The elementwise variants a kernel instantiates.  GPUOS_ALL_EW gets the
+// vector bodies: the precompiled operators, or in the kernel linked with
+// custom expressions the custom slots.  GPUOS_APPLY_EW is the per-element
+// switch of the general and 2-D tile bodies: in the linked kernel the custom
+// slots and the precompiled operators, so that a batch mixing both runs in
+// one launch (its precompiled requests through those bodies).
+#define GPUOS_BUILTIN_EW(M) \
   M(V_ADD) M(V_MUL) M(V_SUB) M(V_DIV0) M(V_DIV) M(V_MAX) M(V_MIN) M(V_POW) \
   M(V_RELU) M(V_SIGMOID) M(V_TANH) M(V_EXP) M(V_LOG) M(V_SQRT) M(V_ABS) \
   M(V_HARDSIGMOID) M(V_HARDSWISH) M(V_GELU) M(V_SIN) M(V_COS) M(V_LEAKY_RELU) \
   M(V_CLAMP) M(V_ELU) M(V_SOFTPLUS) M(V_CLAMP_MIN) M(V_CLAMP_MAX) M(V_COPY)
+#ifdef GPUOS_JIT_LINK
+#define GPUOS_JIT_EW(M) \
+  M(V_JIT_BASE + 0) M(V_JIT_BASE + 1) M(V_JIT_BASE + 2) M(V_JIT_BASE + 3) \
+  M(V_JIT_BASE + 4) M(V_JIT_BASE + 5) M(V_JIT_BASE + 6) M(V_JIT_BASE + 7) \
+  M(V_JIT_BASE + 8) M(V_JIT_BASE + 9) M(V_JIT_BASE + 10) M(V_JIT_BASE + 11) \
+  M(V_JIT_BASE + 12) M(V_JIT_BASE + 13) M(V_JIT_BASE + 14) M(V_JIT_BASE + 15)
+#define GPUOS_ALL_EW(M) GPUOS_JIT_EW(M)
+#define GPUOS_APPLY_EW(M) GPUOS_BUILTIN_EW(M) GPUOS_JIT_EW(M)
+#else
+#define GPUOS_ALL_EW(M) GPUOS_BUILTIN_EW(M)
+#define GPUOS_APPLY_EW(M) GPUOS_BUILTIN_EW(M)
 #endif
 
 __device__ __forceinline__ bool ew_apply1(int v, float A, float B, float& r, float p0, float p1) {
   switch (v) {
-    GPUOS_ALL_EW(GPUOS_CASE1)
+    GPUOS_APPLY_EW(GPUOS_CASE1)
     default: return false;
   }
 }
@@ -111,7 +119,7 @@ __device__ __forceinline__ bool ew_apply1(int v, float A, float B, float& r, flo
 __device__ __forceinline__ bool ew_apply4(int v, float A, float B, float C, float D, float& r,
                                           float p0, float p1) {
   switch (v) {
-    GPUOS_ALL_EW(GPUOS_CASE4)
+    GPUOS_JIT_EW(GPUOS_CASE4)
     default: return false;
   }
 }

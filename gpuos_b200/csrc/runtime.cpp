@@ -1318,7 +1318,10 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   uint32_t* cbp = reinterpret_cast<uint32_t*>(base + cb_off);
   ExtRec* ext = reinterpret_cast<ExtRec*>(base + ext_off);
   uint64_t pf = 0, pc = coff, xi = 0;
-  const bool jit_batch = var[0] >= V_JIT_BASE;  // a batch is all custom or all precompiled
+  // a batch with a custom expression runs in the kernel linked with them,
+  // which has every precompiled body as well
+  bool jit_batch = false;
+  for (uint32_t r = 0; r < n && !jit_batch; ++r) jit_batch = var[r] >= V_JIT_BASE;
   // the persistent worker resolves slot requests itself, from its copy of the
   // jump table, when it starts them
   const bool dev_resolve = opt_.mode == GPUOS_MODE_PERSISTENT && !jit_batch;
@@ -1735,10 +1738,8 @@ uint64_t Executor::flush(bool sync, cudaStream_t stream) {
       while (i < reqs.size()) {
         size_t j = i;
         uint64_t bytes = 256, floats = 0, cnts = 0, chunks = 0;
-        const bool jit = variant_of(reqs[i]) >= V_JIT_BASE;
         while (j < reqs.size() && j - i < cap) {
           const Pending& p = reqs[j];
-          if (j > i && (variant_of(p) >= V_JIT_BASE) != jit) break;
           const uint64_t b = 136 + (p.has_ext ? sizeof(ExtRec) : 0);
           if (j > i && (bytes + b > budget || floats + p.partials > (16ull << 20) / 2 ||
                         cnts + p.counters > (4ull << 20) / 2 ||

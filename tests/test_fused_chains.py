@@ -225,3 +225,37 @@ def test_fused_chain_is_one_request(monkeypatch):
     m = a * b
     want = 1.0 / (1.0 + torch.exp(-m)) + c
     assert torch.allclose(r.cpu(), want, rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["stream", "persistent"])
+def test_mixed_custom_and_precompiled_batch_is_one_launch(mode):
+    """A flush of dependent precompiled, reduction and custom requests runs as
+    one batch (in the kernel linked with the custom expressions), in stage
+    order."""
+    import gpuos_b200.cabi as C
+    g = torch.Generator(device="cpu").manual_seed(74)
+    B, N = 16, 3000
+    x, r, w = torch.randn(B, N, generator=g), torch.randn(B, N, generator=g), torch.randn(N, generator=g)
+    d = {k: v.to(DEV) for k, v in dict(x=x, r=r, w=w).items()}
+    h, sq, o = (torch.empty(B, N, device=DEV) for _ in range(3))
+    m = torch.empty(B, 1, device=DEV)
+    md = C.MODE_STREAM if mode == "stream" else C.MODE_PERSISTENT
+    with C.Executor(0, mode=md) as ex:
+        tail = ex.register_elementwise("mix|tail", "gpuos_keep_f32(A * rsqrtf(B + 1e-6f)) * C", 3)
+        mean = ex.register_reduce("mix|mean", "mean")
+        ex.flush(sync=True)
+        p0 = ex.stats()["published"]
+        ex.builtin(C.OP_ADD, d["x"], d["r"], h)
+        ex.builtin(C.OP_MUL, h, h, sq)
+        ex.reduce(mean, sq, m, [1], True)
+        ex.nary(tail, [h, m, d["w"]], o)
+        ex.flush(sync=True)
+        if md == C.MODE_STREAM:  # (persistent mode runs such a batch on its own launch)
+            assert ex.stats()["published"] - p0 == 1
+    H = x + r
+    assert torch.equal(h.cpu(), H)
+    M = (H * H).double().mean(1, keepdim=True)
+    assert torch.allclose(m.cpu().double(), M, rtol=1e-5, atol=1e-6)
+    want = (H * torch.rsqrt(m.cpu() + 1e-6)) * w
+    assert torch.allclose(o.cpu(), want, rtol=1e-5, atol=1e-6)
