@@ -938,13 +938,13 @@ def bench_reference(args, world, rank):
 def profile_case(dev="cuda:0"):
     """The small case the committed ncu captures use, in stream mode, with a
     256 MB write before each step that evicts its inputs from L2:
-      launches 0-1  the whole add/mul stream (1024 x 4096 fp32; two lean
-                    batches of 512 requests, 25 MB each)
-      launch 2      the first batch of the mixed 24-operator stream (its first
-                    512 requests, seed 0), exactly as the bench runs it
-      launch 3      the first 512 requests of the broadcast stream
-      launch 4      the first 512 requests of the reduction stream
-    About 4 GB on the device."""
+      launch 0  the whole add/mul stream (1024 x 4096 fp32: one lean batch of
+                requests of one shape, 50 MB)
+      launch 1  the first batch of the mixed 24-operator stream (its first
+                512 requests, seed 0), exactly as the bench runs it
+      launch 2  the first 512 requests of the broadcast stream (191 MB)
+      launch 3  the first 64 requests of the reduction stream (about 300 MB)
+    Under 1 GB on the device."""
     import gpuos_b200.cabi as C
     from gpuos_b200 import workloads as W
     scrub = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 2 x L2: evicts the inputs
@@ -954,7 +954,9 @@ def profile_case(dev="cuda:0"):
                                         ("broadcast_mixed", {"fill": False}),
                                         ("lastdim_reduce", {"fill": False}))):
             st = W.STREAMS[name](**kw)
-            if name != "micro_add_mul":
+            if name == "lastdim_reduce":
+                st = st.head(64)
+            elif name != "micro_add_mul":
                 st = st.head(st.flush_every)
             din, dout = st.device_buffers(dev)
             calls = sub.prepare(st, st.views(din, dout))

@@ -35,7 +35,7 @@ class Options(ctypes.Structure):
 class Stats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in (
         "published", "staged", "processed", "retired", "heartbeat", "requests", "pending",
-        "errors", "relaunches", "dev_ns", "lean")] + [(n, ctypes.c_int32) for n in (
+        "errors", "relaunches", "dev_ns", "lean", "chain")] + [(n, ctypes.c_int32) for n in (
             "capacity", "max_batch", "mode", "worker_alive", "quit", "grid", "block", "device")]
 
 

@@ -262,6 +262,67 @@ __device__ __forceinline__ uint32_t warp_batch(const Exec& ex, uint32_t gw, uint
   return count;
 }
 
+// ---- chain batches ---------------------------------------------------------
+// A stream-mode batch with stage barriers that is small (a dependent chain of
+// small requests, e.g. a decode step at batch 1) runs on one thread-block
+// cluster instead of the whole GPU: the cluster's warps split each stage's
+// chunks (warp g of W takes chunks g, g + W, ... of the stage), and a cluster
+// barrier with release / acquire semantics separates the stages.  A stage hop
+// then costs one hardware barrier instead of a fence, an atomic and a polled
+// counter in global memory.  Every CTA of the cluster runs every stage, so
+// the barrier needs no bound.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+// Returns the chunks this warp ran.  The stages are the runs of requests
+// with equal req_wait (their stage's first chunk); requests are in stage order.
+template <int BODIES>
+__device__ __forceinline__ uint32_t chain_batch(const Exec& ex, uint32_t nreq, ExtRec* xs) {
+  const uint32_t W = cluster_size() * kWarpsPerCta;
+  const uint32_t gw = cluster_rank() * kWarpsPerCta + (threadIdx.x >> 5);
+  uint32_t count = 0;
+  Cur cur;
+  uint32_t r0 = 0;
+  while (r0 < nreq) {
+    const uint32_t w0 = __ldcg(ex.req_wait + r0);
+    uint32_t r1 = r0 + 1;
+    while (r1 < nreq && __ldcg(ex.req_wait + r1) == w0) ++r1;
+    const uint32_t s1 = __ldcg(ex.gcb + r1);
+    uint32_t r = r0, rbase = __ldcg(ex.gcb + r0), rend = __ldcg(ex.gcb + r0 + 1);
+    int decoded = -1;
+    for (uint32_t c = rbase + gw; c < s1; c += W) {
+      while (c >= rend) {
+        ++r;
+        rbase = rend;
+        rend = __ldcg(ex.gcb + r + 1);
+      }
+      if ((int)r != decoded) {
+        decode(cur, ex, ex.recs + r, load_req_words(ex.recs + r, ex.lane), xs);
+        decoded = (int)r;
+      }
+      run_chunk<BODIES>(ex, cur, c - rbase, xs);
+      ++count;
+    }
+    cluster_sync_all();
+    r0 = r1;
+  }
+  return count;
+}
+
 // All threads of the CTA, after warp_batch: count the CTA's chunks into the
 // batch (completing it if they are the last), then leave the batch.  The last
 // of `nctas` CTAs to leave zeroes the batch's counters for the slot's next use

@@ -359,9 +359,10 @@ __device__ __forceinline__ void ew_generic_nary(const ReqView& q, const ExtRec* 
 // (row stride 1) is read by each lane along its own contiguous runs, which L1
 // serves for the neighbouring rows.  Each column's operand pointers are set
 // up once per tile and advanced by the row strides: no division and no index
-// multiplication per element.  The dtypes and the operator are template
-// parameters for the broadcast configuration's combinations (-1: read at run
-// time).
+// multiplication per element.  Whole blocks of rows of a tile whose columns
+// are all in range run without per-element bounds checks.  The dtypes and
+// the operator are template parameters for the broadcast configuration's
+// combinations (-1: read at run time).
 // ---------------------------------------------------------------------------
 static constexpr int kTileC = 2;
 static constexpr int kTileR = 4;
@@ -398,13 +399,51 @@ __device__ __forceinline__ float t2_op(int v, float A, float B, float p0, float 
   }
 }
 
+// One block of kTileR rows of a lane's kTileC columns.  CHECK: the last
+// block of a tile, or a tile whose columns run past the chunk: loads and
+// stores are predicated on the row and column being in range.
+template <int DA, int DB, int DO, int V, bool CHECK>
+__device__ __forceinline__ void tile2d_rows(const ReqView& q, int v, float p0, float p1,
+                                            const uint8_t* const* pa, const uint8_t* const* pb,
+                                            uint8_t* const* po, const float* bc, const bool* ok,
+                                            int64_t rows_left, bool hasb, bool b_col,
+                                            int64_t ra_b, int64_t rb_b, int64_t ro_b) {
+  uint32_t ra[kTileR][kTileC], rb[kTileR][kTileC];
+#pragma unroll
+  for (int u = 0; u < kTileR; ++u) {
+#pragma unroll
+    for (int j = 0; j < kTileC; ++j) {
+      ra[u][j] = 0u;
+      rb[u][j] = 0u;
+      if (!CHECK || (ok[j] && u < rows_left)) {
+        ra[u][j] = t2_ld<DA>(pa[j] + u * ra_b, q.dta);
+        if (hasb && !b_col) rb[u][j] = t2_ld<DB>(pb[j] + u * rb_b, q.dtb);
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kTileR; ++u) {
+#pragma unroll
+    for (int j = 0; j < kTileC; ++j) {
+      if (!CHECK || (ok[j] && u < rows_left)) {
+        const float A = t2_cvt<DA>(ra[u][j], q.dta);
+        const float B = hasb ? (b_col ? bc[j] : t2_cvt<DB>(rb[u][j], q.dtb)) : 0.f;
+        t2_st<DO>(po[j] + u * ro_b, q.dto, t2_op<V>(v, A, B, p0, p1));
+      }
+    }
+  }
+}
+
 template <int DA, int DB, int DO, int V>
 __device__ __forceinline__ void ew_tile2d(const ReqView& q, int v, float p0, float p1, uint32_t k,
                                           int lane) {
+  // the broadcast configuration's operators all take B
+  constexpr bool kBin = V == V_ADD || V == V_SUB || V == V_MUL || V == V_DIV0 || V == V_MAX ||
+                        V == V_MIN;
   const int64_t N = q.inner, R = q.nseg;
   const int64_t cb = (int64_t)k * q.chunk;
   const int64_t ce = min(N, cb + (int64_t)q.chunk);
-  const bool hasb = q.flags & RF_HAS_B;
+  const bool hasb = kBin || (q.flags & RF_HAS_B);
   const bool a_sc = q.flags & RF_A_SCALAR, b_sc = q.flags & RF_B_SCALAR;
   const int ea = t2_esz<DA>(q.dta), eb = t2_esz<DB>(q.dtb), eo = t2_esz<DO>(q.dto);
   // byte strides down the rows (0 for a scalar operand)
@@ -412,6 +451,7 @@ __device__ __forceinline__ void ew_tile2d(const ReqView& q, int v, float p0, flo
   const int64_t ro_b = q.so_row * eo;
   // B that does not vary down the rows ([N]) or at all: one value per column
   const bool b_col = hasb && (b_sc || q.sb_row == 0);
+  const int64_t rfull = R - R % kTileR;  // rows in whole blocks
 #pragma unroll 1
   for (int64_t c0 = cb + lane; c0 < ce; c0 += 32 * kTileC) {
     const uint8_t* pa[kTileC];
@@ -429,32 +469,25 @@ __device__ __forceinline__ void ew_tile2d(const ReqView& q, int v, float p0, flo
       po[j] = reinterpret_cast<uint8_t*>(q.o) + cc * eo;
       bc[j] = b_col ? t2_cvt<DB>(t2_ld<DB>(pb[j], q.dtb), q.dtb) : 0.f;
     }
+    const bool all_cols = ok[kTileC - 1];  // columns are in range up to the first that is not
+    int64_t i0 = 0;
+    if (all_cols) {
 #pragma unroll 1
-    for (int64_t i0 = 0; i0 < R; i0 += kTileR) {
-      uint32_t ra[kTileR][kTileC], rb[kTileR][kTileC];
-#pragma unroll
-      for (int u = 0; u < kTileR; ++u) {
-#pragma unroll
-        for (int j = 0; j < kTileC; ++j) {
-          ra[u][j] = 0u;
-          rb[u][j] = 0u;
-          if (ok[j] && i0 + u < R) {
-            ra[u][j] = t2_ld<DA>(pa[j] + u * ra_b, q.dta);
-            if (hasb && !b_col) rb[u][j] = t2_ld<DB>(pb[j] + u * rb_b, q.dtb);
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kTileR; ++u) {
+      for (; i0 < rfull; i0 += kTileR) {
+        tile2d_rows<DA, DB, DO, V, false>(q, v, p0, p1, pa, pb, po, bc, ok, kTileR, hasb, b_col,
+                                          ra_b, rb_b, ro_b);
 #pragma unroll
         for (int j = 0; j < kTileC; ++j) {
-          if (ok[j] && i0 + u < R) {
-            const float A = t2_cvt<DA>(ra[u][j], q.dta);
-            const float B = hasb ? (b_col ? bc[j] : t2_cvt<DB>(rb[u][j], q.dtb)) : 0.f;
-            t2_st<DO>(po[j] + u * ro_b, q.dto, t2_op<V>(v, A, B, p0, p1));
-          }
+          pa[j] += kTileR * ra_b;
+          pb[j] += kTileR * rb_b;
+          po[j] += kTileR * ro_b;
         }
       }
+    }
+#pragma unroll 1
+    for (; i0 < R; i0 += kTileR) {
+      tile2d_rows<DA, DB, DO, V, true>(q, v, p0, p1, pa, pb, po, bc, ok, R - i0, hasb, b_col,
+                                       ra_b, rb_b, ro_b);
 #pragma unroll
       for (int j = 0; j < kTileC; ++j) {
         pa[j] += kTileR * ra_b;

@@ -288,6 +288,7 @@ PyObject* stats_dict(const gpuos_stats& s, bool reference_keys_only) {
     put("relaunches", PyLong_FromUnsignedLongLong(s.relaunches));
     put("dev_ns", PyLong_FromUnsignedLongLong(s.dev_ns));
     put("lean", PyLong_FromUnsignedLongLong(s.lean));
+    put("chain", PyLong_FromUnsignedLongLong(s.chain));
     put("worker_alive", PyBool_FromLong(s.worker_alive));
     put("grid", PyLong_FromLong(s.grid));
     put("block", PyLong_FromLong(s.block));

@@ -300,6 +300,22 @@ struct LeanBatch {
   LeanRec  rec[N];
 };
 
+// A lean batch of up to 1024 requests of one shape (the same element count
+// and chunk length, e.g. the add/mul stream): no chunk prefix, and 26 bytes
+// per request, so twice as many requests fit the parameter space.
+static constexpr int kLeanUniMax = 1024;
+struct LeanUniBatch {
+  LeanHdr  h;
+  uint32_t numel;        // every request's elements (< 2^31)
+  uint32_t chunk;        // elements per chunk (a multiple of 4)
+  uint32_t kpr;          // chunks per request
+  uint32_t pad;
+  uint64_t a[kLeanUniMax], b[kLeanUniMax], o[kLeanUniMax];
+  uint8_t  op[kLeanUniMax];
+  uint8_t  pidx[kLeanUniMax];
+};
+static_assert(sizeof(LeanUniBatch) <= 32764, "kernel parameter space");
+
 // Arguments of the persistent worker kernel.
 struct WorkerArgs {
   uint8_t* ring;                 // device staging ring

@@ -32,6 +32,12 @@ gpuos_lean_kernel(const __grid_constant__ LeanBatch<N> bt) {
   lean_batch<N, kLeanThreads, 4>(bt);
 }
 
+// Up to 1024 requests of one shape in one parameter block (LeanUniBatch).
+__global__ void __launch_bounds__(kLeanThreads, 2)
+gpuos_lean_uni_kernel(const __grid_constant__ LeanUniBatch bt) {
+  lean_uni_batch<kLeanThreads, 4>(bt);
+}
+
 // The batch's descriptors are in the device staging ring (payload); its
 // counters are `st`, one slot of a device array.  BODIES selects the chunk
 // bodies the kernel carries (process_chunk).
@@ -78,6 +84,20 @@ extern "C" __global__ void __launch_bounds__(kCtaThreads, kMinCtasPerSm)
 gpuos_batch_red_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
                        volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
   batch_body<BODY_RED>(payload, hdr, st, done_ring, wait_limit_ns);
+}
+
+// A small batch with stage barriers on one thread-block cluster (chain_batch
+// in batch.cuh); launched with a cluster dimension equal to the grid.
+extern "C" __global__ void __launch_bounds__(kCtaThreads, 1)
+gpuos_chain_kernel(const uint8_t* payload, const BatchHdr hdr, BatchState* st,
+                   volatile uint64_t* done_ring, uint64_t wait_limit_ns) {
+  __shared__ ExtRec ext[kWarpsPerCta];
+  __shared__ uint32_t cta_chunks;
+  if (threadIdx.x == 0) cta_chunks = 0;
+  __syncthreads();
+  const Exec ex = bind_batch(payload, hdr, st, done_ring, nullptr, wait_limit_ns);
+  const uint32_t count = chain_batch<BODY_ALL>(ex, hdr.nreq, &ext[threadIdx.x >> 5]);
+  cta_leave_batch(ex, &cta_chunks, count, gridDim.x, nullptr);
 }
 
 // Copy `bytes` (multiple of 16, both ends 16-byte aligned) from mapped host
@@ -239,6 +259,26 @@ extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::B
   return cudaGetLastError();
 }
 
+// One cluster of `ctas` CTAs (at most 8, the portable cluster size).
+extern "C" cudaError_t gpuos_launch_chain(const uint8_t* payload, const gpuos::BatchHdr* hdr,
+                                          gpuos::BatchState* st, volatile uint64_t* done_ring,
+                                          uint64_t wait_limit_ns, int ctas, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(gpuos::kCtaThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = (unsigned)ctas;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gpuos::gpuos_chain_kernel, payload, *hdr, st, done_ring,
+                            wait_limit_ns);
+}
+
 extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, cudaStream_t stream) {
   const gpuos::WorkerArgs* w = static_cast<const gpuos::WorkerArgs*>(args);
   gpuos::gpuos_worker_kernel<<<grid, gpuos::kCtaThreads, 0, stream>>>(*w);
@@ -269,6 +309,9 @@ extern "C" cudaError_t gpuos_launch_lean(const void* params, int size_class, int
     case 2:
       return cudaLaunchKernelEx(&cfg, gpuos::gpuos_lean_kernel<gpuos::kLeanMaxReq>,
                                 *static_cast<const gpuos::LeanBatch<gpuos::kLeanMaxReq>*>(params));
+    case 3:
+      return cudaLaunchKernelEx(&cfg, gpuos::gpuos_lean_uni_kernel,
+                                *static_cast<const gpuos::LeanUniBatch*>(params));
     default:
       return cudaErrorInvalidValue;
   }
@@ -279,6 +322,7 @@ extern "C" size_t gpuos_lean_params_size(int size_class) {
     case 0: return sizeof(gpuos::LeanBatch<32>);
     case 1: return sizeof(gpuos::LeanBatch<128>);
     case 2: return sizeof(gpuos::LeanBatch<gpuos::kLeanMaxReq>);
+    case 3: return sizeof(gpuos::LeanUniBatch);
     default: return 0;
   }
 }

@@ -27,6 +27,9 @@
 //     complete in stream order.
 //   * completion: the last CTA posts the batch's completion word (seq + 1)
 //     to mapped host memory.
+// A batch of up to 1024 requests of one shape (LeanUniBatch: the add/mul
+// stream's 1024 x 4096 in one launch instead of two) has no chunk prefix:
+// chunk c belongs to request c / kpr.
 #pragma once
 #include "executor.cuh"
 
@@ -53,13 +56,13 @@ struct LeanCur {
 };
 
 // elements [e0, e0 + n) of one request, n > 0 (unary operators ignore b)
-template <int V, int N, int GL>
-__device__ __forceinline__ void lean_chunk(const LeanCur& u, const LeanBatch<N>& bt, uint32_t e0,
+template <int V, int GL>
+__device__ __forceinline__ void lean_chunk(const LeanCur& u, const LeanHdr& h, uint32_t e0,
                                            uint32_t n, int lane) {
   constexpr int kG = lean_groups<V, GL>();
   constexpr bool kBin = V == V_ADD || V == V_MUL || V == V_SUB || V == V_DIV0 || V == V_DIV ||
                         V == V_MAX || V == V_MIN || V == V_POW;
-  const float p0 = bt.h.par[u.pidx][0], p1 = bt.h.par[u.pidx][1];
+  const float p0 = h.par[u.pidx][0], p1 = h.par[u.pidx][1];
   const uint32_t nq = n >> 2;
   const float4* A = reinterpret_cast<const float4*>(u.a + e0);
   const float4* B = reinterpret_cast<const float4*>(u.b + e0);
@@ -94,15 +97,37 @@ __device__ __forceinline__ void lean_chunk(const LeanCur& u, const LeanBatch<N>&
   }
 }
 
-#define GPUOS_LEAN_CASE(V) case V: lean_chunk<V, N, GL>(u, bt, e0, n, lane); return;
+#define GPUOS_LEAN_CASE(V) case V: lean_chunk<V, GL>(u, h, e0, n, lane); return;
 
-template <int N, int GL>
-__device__ __forceinline__ void lean_dispatch(const LeanCur& u, const LeanBatch<N>& bt, uint32_t e0,
+template <int GL>
+__device__ __forceinline__ void lean_dispatch(const LeanCur& u, const LeanHdr& h, uint32_t e0,
                                               uint32_t n, int lane) {
   switch (u.op) {
     GPUOS_ALL_EW(GPUOS_LEAN_CASE)
     default: return;
   }
+}
+
+// End of a lean batch: every CTA releases its stores, the last one posts the
+// batch's duration and completion word; the grid completes only after the
+// previous grid in the stream has (stream order).
+__device__ __forceinline__ void lean_finish(const LeanHdr& h, BatchState* st) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t left = atomicAdd(&st->ctas_left, 1u) + 1u;
+    if (left == gridDim.x) {
+      __threadfence();
+      const uint64_t nt0 = *reinterpret_cast<volatile uint64_t*>(&st->nt0);
+      st->nt0 = 0ull;
+      st->ctas_left = 0u;
+      reinterpret_cast<volatile uint64_t*>(h.dur_ring)[h.seq % kDoneRing] =
+          nt0 ? globaltimer() - ~nt0 : 0ull;
+      volatile uint64_t* dr = reinterpret_cast<volatile uint64_t*>(h.done_ring);
+      st_release_sys_u64(&dr[h.seq % kDoneRing], h.seq + 1);
+    }
+  }
+  gdc_wait();
 }
 
 template <int N>
@@ -161,26 +186,46 @@ __device__ __forceinline__ void lean_batch(const LeanBatch<N>& bt) {
     }
     const uint32_t e0 = (c - rbase) * u.chunk;
     const uint32_t n = min(u.chunk, u.numel - e0);
-    lean_dispatch<N, GL>(u, bt, e0, n, lane);
+    lean_dispatch<GL>(u, h, e0, n, lane);
   }
-  // completion: every CTA releases its stores, the last one posts the word
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t left = atomicAdd(&st->ctas_left, 1u) + 1u;
-    if (left == gridDim.x) {
-      __threadfence();
-      const uint64_t nt0 = *reinterpret_cast<volatile uint64_t*>(&st->nt0);
-      st->nt0 = 0ull;
-      st->ctas_left = 0u;
-      reinterpret_cast<volatile uint64_t*>(h.dur_ring)[h.seq % kDoneRing] =
-          nt0 ? globaltimer() - ~nt0 : 0ull;
-      volatile uint64_t* dr = reinterpret_cast<volatile uint64_t*>(h.done_ring);
-      st_release_sys_u64(&dr[h.seq % kDoneRing], h.seq + 1);
+  lean_finish(h, st);
+}
+
+// A batch of requests of one shape (LeanUniBatch): chunk c is chunk
+// c mod kpr of request c / kpr; otherwise as lean_batch.
+template <int THREADS, int GL>
+__device__ __forceinline__ void lean_uni_batch(const LeanUniBatch& bt) {
+  const LeanHdr& h = bt.h;
+  gdc_launch_dependents();
+  BatchState* st = reinterpret_cast<BatchState*>(h.st);
+  if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned long long*>(&st->nt0), ~globaltimer());
+  const int lane = threadIdx.x & 31;
+  constexpr uint32_t kWarps = THREADS / 32;
+  const uint64_t W = (uint64_t)gridDim.x * kWarps;
+  const uint64_t gw = (uint64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  const uint32_t nchunk = h.nchunk, kpr = bt.kpr;
+  const uint32_t c0 = (uint32_t)(gw * nchunk / W);
+  const uint32_t c1 = (uint32_t)((gw + 1) * nchunk / W);
+  if (h.flags & LEAN_WAIT_FIRST) gdc_wait();
+  LeanCur u;
+  u.numel = bt.numel;
+  u.chunk = bt.chunk;
+  uint32_t r = c0 / kpr, k = c0 - r * kpr;
+  for (uint32_t c = c0; c < c1; ++c) {
+    u.a = reinterpret_cast<const float*>(bt.a[r]);
+    u.b = reinterpret_cast<const float*>(bt.b[r]);
+    u.o = reinterpret_cast<float*>(bt.o[r]);
+    u.op = bt.op[r];
+    u.pidx = bt.pidx[r];
+    const uint32_t e0 = k * u.chunk;
+    lean_dispatch<GL>(u, h, e0, min(u.chunk, u.numel - e0), lane);
+    if (++k == kpr) {
+      k = 0;
+      ++r;
     }
   }
-  // complete only after the previous grid in the stream has (stream order)
-  gdc_wait();
+  lean_finish(h, st);
 }
+
 
 }  // namespace gpuos

@@ -25,6 +25,9 @@ extern "C" cudaError_t gpuos_launch_batch(const uint8_t* payload, const gpuos::B
                                           uint64_t wait_limit_ns, int grid, cudaStream_t stream,
                                           int bodies);
 extern "C" cudaError_t gpuos_launch_worker(const void* args, int grid, cudaStream_t stream);
+extern "C" cudaError_t gpuos_launch_chain(const uint8_t* payload, const gpuos::BatchHdr* hdr,
+                                          gpuos::BatchState* st, volatile uint64_t* done_ring,
+                                          uint64_t wait_limit_ns, int ctas, cudaStream_t stream);
 extern "C" cudaError_t gpuos_occupancy(int* batch_blocks_per_sm, int* worker_blocks_per_sm,
                                        int* ew_blocks_per_sm, int* red_blocks_per_sm);
 extern "C" int gpuos_cta_threads();
@@ -380,8 +383,9 @@ Executor::Executor(int device, const gpuos_options& opt) : device_(device), opt_
   total_warps_ = ctas * gpuos_cta_threads() / 32;
   lean_grid_ = sm_count_;
   lean_on_ = env_double("GPUOS_LEAN", 1.0) != 0.0;
+  chain_on_ = env_double("GPUOS_CHAIN", 1.0) != 0.0;
   lean_warps_ = sm_count_ * kLeanThreads / 32;
-  lean_buf_.resize(gpuos_lean_params_size(2));
+  lean_buf_.resize(std::max(gpuos_lean_params_size(2), gpuos_lean_params_size(3)));
 
   GCU(cudaStreamCreateWithFlags(&s_worker_, cudaStreamNonBlocking));
   GCU(cudaStreamCreateWithFlags(&s_ctrl_, cudaStreamNonBlocking));
@@ -1160,7 +1164,7 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   // (at least 128 elements).
   std::vector<int> var(n);
   std::vector<uint8_t> cost_log2(n);  // every cost is a power of two
-  uint64_t ew_work = 0;
+  uint64_t ew_work = 0, est_bytes = 0;
   for (uint32_t r = 0; r < n; ++r) {
     Pending& p = reqs[i + r];
     int v = p.r.op;
@@ -1173,10 +1177,13 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
     if (p.r.kind == RK_EW) {
       cost_log2[r] = (uint8_t)__builtin_ctzll(ew_cost(p, v));
       ew_work += (uint64_t)p.r.numel << cost_log2[r];
+      est_bytes += (uint64_t)p.r.numel * 12u;
+    } else {
+      est_bytes += (uint64_t)p.r.numel * (uint64_t)p.r.inner * 4u;
     }
   }
   // a lean batch: the whole batch in the lean kernel's parameters (lean.cuh)
-  bool lean = lean_on_ && opt_.mode == GPUOS_MODE_STREAM && !staged && n <= (uint32_t)kLeanMaxReq;
+  bool lean = lean_on_ && opt_.mode == GPUOS_MODE_STREAM && !staged && n <= (uint32_t)kLeanUniMax;
   for (uint32_t r = 0; r < n && lean; ++r) lean = lean_eligible(reqs[i + r], var[r]);
   if (lean) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -1369,13 +1376,16 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       }
     }
   }
+  bool stalled = false;
   if (staged) {
     uint32_t* w = reinterpret_cast<uint32_t*>(base + wait_off);
     for (uint32_t r = 0; r < n; ++r) w[r] = stage_first[r] ? cb[stage_first[r]] : 0u;
     if (stall_next_) {
       // fault injection: the last stage waits for one chunk more than the
       // earlier stages have, which only its own (waiting) chunks could add
+      // (on the polled stage barriers: such a batch does not run as a chain)
       stall_next_ = false;
+      stalled = true;
       const uint32_t last = stage_first[n - 1];
       for (uint32_t r = 0; r < n; ++r)
         if (stage_first[order[r]] == last) w[r] = cb[last] + 1u;
@@ -1449,9 +1459,17 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
       }
       GCU(cudaEventRecord(e0, stream));
     }
+    // A small batch with stage barriers (at most 32 MB, counting 12 bytes an
+    // elementwise element and 4 a reduced one) runs on one cluster of 8 CTAs
+    // with cluster barriers between its stages (chain_batch).
+    const bool chain = staged && !stalled && !jit_batch && chain_on_ && est_bytes <= (32ull << 20);
     if (jit_batch) {
       jit_launch(jit_kernels_.back(), grid, block_, stream, ring_ + aoff, *h,
                  states_ + seq % kDoneRing, dr, wait_limit_ns_);
+    } else if (chain) {
+      GCU(gpuos_launch_chain(ring_ + aoff, h, states_ + seq % kDoneRing, dr, wait_limit_ns_, 8,
+                             stream));
+      ++chain_count_;
     } else {
       GCU(gpuos_launch_batch(ring_ + aoff, h, states_ + seq % kDoneRing, dr, wait_limit_ns_, grid,
                              stream, bodies));
@@ -1536,6 +1554,45 @@ void fill_lean(uint8_t* buf, uint64_t seq, uint64_t st, uint64_t done_ring, uint
 // A request the lean kernel can run: contiguous, 16-byte aligned fp32 tensors
 // (no scalar operands) of a precompiled elementwise operator, with B present
 // when the operator reads it.
+// The parameter block of a batch of requests of one shape (LeanUniBatch).
+void fill_lean_uni(uint8_t* buf, uint64_t seq, uint64_t st, uint64_t done_ring, uint64_t dur_ring,
+                   uint32_t flags, const std::vector<Pending>& reqs, size_t i, uint32_t n,
+                   const std::vector<int>& var, const std::vector<uint32_t>& order,
+                   uint64_t nchunk, const Tables& tab) {
+  LeanUniBatch* b = reinterpret_cast<LeanUniBatch*>(buf);
+  std::memset(&b->h, 0, sizeof(b->h));
+  b->h.seq = seq;
+  b->h.st = st;
+  b->h.done_ring = done_ring;
+  b->h.dur_ring = dur_ring;
+  b->h.nreq = n;
+  b->h.nchunk = (uint32_t)nchunk;
+  b->h.flags = flags;
+  const Pending& p0 = reqs[i];
+  b->numel = (uint32_t)p0.r.numel;
+  b->chunk = p0.r.chunk;
+  b->kpr = p0.nchunk;
+  b->pad = 0;
+  int npar = 0;
+  for (uint32_t r = 0; r < n; ++r) {
+    const Pending& p = reqs[i + order[r]];
+    float p0v, p1v;
+    effective_params(tab, p.r, &p0v, &p1v);
+    int k = 0;
+    while (k < npar && !(b->h.par[k][0] == p0v && b->h.par[k][1] == p1v)) ++k;
+    if (k == npar) {
+      b->h.par[k][0] = p0v;
+      b->h.par[k][1] = p1v;
+      ++npar;
+    }
+    b->a[r] = p.r.a;
+    b->b[r] = p.r.b;
+    b->o[r] = p.r.o;
+    b->op[r] = (uint8_t)var[order[r]];
+    b->pidx[r] = (uint8_t)k;
+  }
+}
+
 bool Executor::lean_eligible(const Pending& p, int v) const {
   const Req& q = p.r;
   if (q.kind != RK_EW || q.layout != EL_CONTIG || !(q.flags & RF_VEC) || p.has_ext) return false;
@@ -1565,6 +1622,17 @@ bool Executor::publish_lean(std::unique_lock<std::mutex>& lk, std::vector<Pendin
     }
   }
   if (nchunk == 0 || nchunk > 0x7fffffffull) return false;
+  // more requests than a LeanBatch holds: only as requests of one shape
+  bool uni = false;
+  if (n > (uint32_t)kLeanMaxReq) {
+    const Pending& p0 = reqs[i];
+    uni = n <= (uint32_t)kLeanUniMax;
+    for (uint32_t r = 1; r < n && uni; ++r) {
+      const Pending& p = reqs[i + r];
+      uni = p.r.numel == p0.r.numel && p.r.chunk == p0.r.chunk && p.nchunk == p0.nchunk;
+    }
+    if (!uni) return false;
+  }
   // a free batch slot (counters and completion word)
   const auto t0 = std::chrono::steady_clock::now();
   for (int it = 0;; ++it) {
@@ -1587,7 +1655,7 @@ bool Executor::publish_lean(std::unique_lock<std::mutex>& lk, std::vector<Pendin
     wf = lean_out_.overlaps(p.out_ext) || lean_in_.overlaps(p.out_ext);
     for (int k = 0; k < p.nin && !wf; ++k) wf = lean_out_.overlaps(p.in_ext[k]);
   }
-  const int cls = n <= 32 ? 0 : (n <= 128 ? 1 : 2);
+  const int cls = uni ? 3 : n <= 32 ? 0 : (n <= 128 ? 1 : 2);
   const uint64_t st = reinterpret_cast<uint64_t>(states_ + seq % kDoneRing);
   const uint64_t dr = reinterpret_cast<uint64_t>(
       hostblk_dev_ + (reinterpret_cast<const volatile uint8_t*>(done_ring_) - hostblk_));
@@ -1597,7 +1665,8 @@ bool Executor::publish_lean(std::unique_lock<std::mutex>& lk, std::vector<Pendin
   uint8_t* buf = lean_buf_.data();
   if (cls == 0) fill_lean<32>(buf, seq, st, dr, du, flags, reqs, i, n, var, order, nchunk, tab_);
   else if (cls == 1) fill_lean<128>(buf, seq, st, dr, du, flags, reqs, i, n, var, order, nchunk, tab_);
-  else fill_lean<kLeanMaxReq>(buf, seq, st, dr, du, flags, reqs, i, n, var, order, nchunk, tab_);
+  else if (cls == 2) fill_lean<kLeanMaxReq>(buf, seq, st, dr, du, flags, reqs, i, n, var, order, nchunk, tab_);
+  else fill_lean_uni(buf, seq, st, dr, du, flags, reqs, i, n, var, order, nchunk, tab_);
   dur_ring_[seq % kDoneRing] = 0;
   DeviceGuard g(device_);
   if (have_last_stream_ && stream != last_stream_ && done_wm_ < seq) {
@@ -1732,13 +1801,32 @@ uint64_t Executor::flush(bool sync, cudaStream_t stream) {
       lean_out_.clear();
       lean_in_.clear();
       // stream mode: batches no larger than a lean parameter block holds
-      const size_t cap = (opt_.mode == GPUOS_MODE_STREAM && lean_on_)
-                             ? std::min<size_t>(opt_.max_batch, kLeanMaxReq)
-                             : (size_t)opt_.max_batch;
+      const bool lean_mode = opt_.mode == GPUOS_MODE_STREAM && lean_on_;
+      const size_t cap = lean_mode ? std::min<size_t>(opt_.max_batch, kLeanMaxReq)
+                                   : (size_t)opt_.max_batch;
       while (i < reqs.size()) {
         size_t j = i;
         uint64_t bytes = 256, floats = 0, cnts = 0, chunks = 0;
-        while (j < reqs.size() && j - i < cap) {
+        // A run of lean requests of one shape (element count and operator
+        // cost class, so one chunk length) fills a batch of up to 1024: its
+        // parameter block (LeanUniBatch) holds twice as many requests.
+        size_t cap_i = cap;
+        if (lean_mode && opt_.max_batch >= kLeanMaxReq) {
+          const Pending& p0 = reqs[i];
+          const int v0 = variant_of(p0);
+          size_t k = i;
+          if (lean_eligible(p0, v0))
+            while (k < reqs.size() && k - i < (size_t)kLeanUniMax) {
+              const Pending& p = reqs[k];
+              const int v = variant_of(p);
+              if (p.r.numel != p0.r.numel || !lean_eligible(p, v) ||
+                  chunk_weight(v) != chunk_weight(v0))
+                break;
+              ++k;
+            }
+          if (k - i > cap) cap_i = k - i;
+        }
+        while (j < reqs.size() && j - i < cap_i) {
           const Pending& p = reqs[j];
           const uint64_t b = 136 + (p.has_ext ? sizeof(ExtRec) : 0);
           if (j > i && (bytes + b > budget || floats + p.partials > (16ull << 20) / 2 ||
@@ -2024,6 +2112,7 @@ void Executor::stats(gpuos_stats* out) {
   out->relaunches = relaunches_;
   out->dev_ns = dev_ns_;
   out->lean = lean_count_;
+  out->chain = chain_count_;
   out->capacity = opt_.capacity;
   out->max_batch = opt_.max_batch;
   out->mode = opt_.mode;

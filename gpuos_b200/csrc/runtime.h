@@ -242,6 +242,8 @@ class Executor {
   // lean batches (stream mode): whole batch in the kernel's parameters, launched
   // with programmatic dependent launch, completed by a word in done_ring_
   bool lean_on_ = true;
+  bool chain_on_ = true;      // small staged batches on one cluster (GPUOS_CHAIN=0: off)
+  uint64_t chain_count_ = 0;  // batches run that way
   int lean_grid_ = 0;                 // CTAs of the lean kernel (one per SM)
   int lean_warps_ = 0;                // warps of a full lean grid
   std::vector<uint8_t> lean_seq_ = std::vector<uint8_t>(kDoneRing, 0);  // batch seq is lean

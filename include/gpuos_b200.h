@@ -88,6 +88,7 @@ typedef struct gpuos_stats {
   uint64_t dev_ns;      /* device time of completed batches, ns: first CTA in -> last chunk
                            (persistent worker and lean batches) */
   uint64_t lean;        /* stream-mode batches run by the lean kernel (parameters only) */
+  uint64_t chain;       /* stream-mode batches with stage barriers run on one cluster */
   int32_t capacity;
   int32_t max_batch;
   int32_t mode;

@@ -773,3 +773,35 @@ def test_decode_chain_bf16(mode, B):
             compare("sigmoid", c["u"], None, c["gt"])
             compare("mul", c["gt"], c["u2"], c["act"])
             assert not torch.isnan(c["xo"].float()).any()
+
+
+@pytest.mark.parametrize("numel", [4096, 1000])
+def test_uniform_lean_batch(numel):
+    """1024 requests of one shape and light operators flushed at once run as
+    one lean launch of the one-shape parameter block (LeanUniBatch); a
+    request of another shape, or a heavier operator, ends the run."""
+    ops = [C.OP_ADD, C.OP_MUL, C.OP_SUB]
+    g = torch.Generator(device="cpu").manual_seed(81)
+    a = torch.randn(1024, numel, generator=g)
+    b = torch.randn(1024, numel, generator=g)
+    da, db = a.to(DEV), b.to(DEV)
+    out = torch.empty(1024, numel, device=DEV)
+    with C.Executor(0, mode=C.MODE_STREAM) as ex:
+        l0 = ex.stats()["lean"]
+        for r in range(1024):
+            ex.builtin(ops[r % 3], da[r], db[r], out[r])
+        ex.flush(sync=True)
+        assert ex.stats()["lean"] - l0 == 1
+        # 1023 of one shape, then one longer request: two batches
+        out2 = torch.empty(1024 * numel + 4, device=DEV)
+        for r in range(1023):
+            ex.builtin(C.OP_ADD, da[r], db[r], out2[r * numel:(r + 1) * numel])
+        big_a = torch.randn(numel + 4, generator=g)
+        ex.builtin(C.OP_MUL, big_a.to(DEV), big_a.to(DEV), out2[1023 * numel:])
+        ex.flush(sync=True)
+        assert ex.stats()["lean"] - l0 == 3
+    want = torch.stack([a[r] + b[r] if r % 3 == 0 else a[r] * b[r] if r % 3 == 1 else a[r] - b[r]
+                        for r in range(1024)])
+    assert torch.equal(out.cpu(), want)
+    assert torch.equal(out2[:1023 * numel].cpu(), (a[:1023] + b[:1023]).reshape(-1))
+    assert torch.equal(out2[1023 * numel:].cpu(), big_a * big_a)
