@@ -829,7 +829,7 @@ def bench_ours(args, world, rank, local):
     chain = decode_chain(ext, dev) if rank == 0 else None
     ext.shutdown()
     pers = persistent_leg(ext, stream, din, dout, max(2, min(args.steps, 5)), world) \
-        if args.mode == "stream" else None
+        if args.mode == "stream" and not args.no_persistent else None
 
     peak, peak_kind = peaks()
     rsteps = max(2, min(args.steps, 5))
@@ -985,7 +985,10 @@ def main():
     ap.add_argument("--no-by-workload", action="store_true",
                     help="time only the headline stream's batch kernel in the roofline leg")
     ap.add_argument("--profile-case", action="store_true",
-                    help="run the small two-launch case of the committed ncu captures and exit")
+                    help="run the small four-launch case of the committed ncu captures and exit")
+    ap.add_argument("--no-persistent", action="store_true",
+                    help="skip the persistent-worker leg (for a profiler that serialises "
+                         "launches: the resident worker waits for the host that launched it)")
     args = ap.parse_args()
     if args.profile_case:
         profile_case()
