@@ -288,37 +288,75 @@ __device__ __forceinline__ uint32_t cluster_size() {
   return r;
 }
 
+// The first request of [r0, nreq) whose req_wait differs from r0's (the end
+// of r0's stage).
+__device__ __forceinline__ uint32_t chain_stage_end(const Exec& ex, uint32_t r0, uint32_t nreq) {
+  const uint32_t w0 = __ldcg(ex.req_wait + r0);
+  uint32_t r1 = r0 + 1;
+  while (r1 < nreq && __ldcg(ex.req_wait + r1) == w0) ++r1;
+  return r1;
+}
+
 // Returns the chunks this warp ran.  The stages are the runs of requests
-// with equal req_wait (their stage's first chunk); requests are in stage order.
+// with equal req_wait (their stage's first chunk); requests are in stage
+// order.  The batch's records do not depend on the data, so each warp loads
+// the record of its first chunk of the next stage before the barrier, and a
+// request that is not on the vector path runs from the record words already
+// in registers: after a barrier a chunk's first global load is its data.
 template <int BODIES>
 __device__ __forceinline__ uint32_t chain_batch(const Exec& ex, uint32_t nreq, ExtRec* xs) {
   const uint32_t W = cluster_size() * kWarpsPerCta;
   const uint32_t gw = cluster_rank() * kWarpsPerCta + (threadIdx.x >> 5);
   uint32_t count = 0;
   Cur cur;
-  uint32_t r0 = 0;
+  uint32_t r0 = 0, r1 = nreq ? chain_stage_end(ex, 0, nreq) : 0;
+  // this warp's first chunk of the stage, its request and record words
+  uint32_t cf = 0, rf = 0;
+  uint4 wf = make_uint4(0u, 0u, 0u, 0u);
+  auto ahead = [&]() {
+    cf = __ldcg(ex.gcb + r0) + gw;
+    rf = r0;
+    if (cf < __ldcg(ex.gcb + r1)) {
+      while (__ldcg(ex.gcb + rf + 1) <= cf) ++rf;
+      wf = load_req_words(ex.recs + rf, ex.lane);
+    }
+  };
+  if (nreq) ahead();
   while (r0 < nreq) {
-    const uint32_t w0 = __ldcg(ex.req_wait + r0);
-    uint32_t r1 = r0 + 1;
-    while (r1 < nreq && __ldcg(ex.req_wait + r1) == w0) ++r1;
     const uint32_t s1 = __ldcg(ex.gcb + r1);
-    uint32_t r = r0, rbase = __ldcg(ex.gcb + r0), rend = __ldcg(ex.gcb + r0 + 1);
+    uint32_t r = rf, rbase = __ldcg(ex.gcb + rf), rend = __ldcg(ex.gcb + rf + 1);
+    uint4 words = wf;
+    bool have = true;  // `words` are request r's
     int decoded = -1;
-    for (uint32_t c = rbase + gw; c < s1; c += W) {
+    for (uint32_t c = cf; c < s1; c += W) {
       while (c >= rend) {
         ++r;
         rbase = rend;
         rend = __ldcg(ex.gcb + r + 1);
+        have = false;
       }
       if ((int)r != decoded) {
-        decode(cur, ex, ex.recs + r, load_req_words(ex.recs + r, ex.lane), xs);
+        if (!have) words = load_req_words(ex.recs + r, ex.lane);
+        have = true;
+        decode(cur, ex, ex.recs + r, words, xs);
         decoded = (int)r;
       }
-      run_chunk<BODIES>(ex, cur, c - rbase, xs);
+      if constexpr ((BODIES & BODY_EW) != 0) {
+        if (cur.vec) {
+          run_chunk<BODIES>(ex, cur, c - rbase, xs);
+          ++count;
+          continue;
+        }
+      }
+      process_chunk<BODIES>(ex, decode_req(words), cur.v, cur.p0, cur.p1, c - rbase, xs);
       ++count;
     }
-    cluster_sync_all();
     r0 = r1;
+    if (r0 < nreq) {
+      r1 = chain_stage_end(ex, r0, nreq);
+      ahead();
+    }
+    cluster_sync_all();
   }
   return count;
 }
