@@ -1202,6 +1202,8 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   if (staged) {
     std::vector<uint64_t> sw(n, 0);
     for (uint32_t r = 0; r < n; ++r)
+      // (elementwise work only: reduction chunks are sized per request, by
+      // build_reduce, whatever else shares their stage)
       if (reqs[i + r].r.kind == RK_EW) sw[stage_first[r]] += (uint64_t)reqs[i + r].r.numel << cost_log2[r];
     stage_ce.resize(n);
     for (uint32_t r = 0; r < n; ++r) {
@@ -1289,6 +1291,9 @@ void Executor::publish(std::unique_lock<std::mutex>& lk, std::vector<Pending>& r
   // (dtypes, layouts) even out across warps; at that size the claims (one
   // atomic per granule of up to 8 chunks) are noise.
   const bool claim = !staged && nchunk >= 16 * warps_all;
+  // claimed granules small enough for about 32 claims per warp: the last
+  // granule a warp claims is the batch's tail
+  if (claim) gran = std::min<uint64_t>(std::max<uint64_t>(nchunk / (32 * warps_all), 1), 8);
   const uint64_t ngran = (nchunk + gran - 1) / gran;
   const uint64_t rec_off = sizeof(BatchHdr);
   const uint64_t cb_off = rec_off + 128ull * n;
