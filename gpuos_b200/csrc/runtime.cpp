@@ -767,8 +767,9 @@ void build_reduce(Pending& p, int op, bool is_slot, const gpuos_tensor& x,
   q.o = reinterpret_cast<uint64_t>(out.data);
   q.nseg = 1;
   const int e = esz(x.dtype);
-  // elements per chunk (or per segment of a long row): 32 KB of input
-  const int64_t kSeg = 32768 / e;
+  // elements per chunk (or per segment of a long row): 64 KB of input
+  // (measured on the reduction stream: 0.575 of HBM against 0.549 with 32 KB)
+  const int64_t kSeg = 65536 / e;
 
   if (mk <= 1 && mr <= 1) {
     const int64_t sr = mk ? ck[0].sa : 0, so = mk ? ck[0].so : 0;

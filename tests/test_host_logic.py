@@ -126,7 +126,7 @@ def test_plan_reductions():
     p = C.plan_reduce(C.variant("sum"), x, torch.empty(100, 1), [-1], True)
     assert (p["kind"], p["layout"], p["nseg"], p["inner"], p["numel"]) == (1, 0, 1, 3000, 100)
     assert p["flags"] & 2 and p["rg"] == 32
-    p = C.plan_reduce(C.variant("sum"), torch.randn(5, 20000), torch.empty(5), [1], False)
+    p = C.plan_reduce(C.variant("sum"), torch.randn(5, 40000), torch.empty(5), [1], False)
     assert p["nseg"] == 3 and p["nchunk"] == 15 and p["partials"] == 15 and p["counters"] == 5
     p = C.plan_reduce(C.variant("sum"), torch.randn(64, 64), torch.empty(64), [1], False)
     assert p["rg"] == 4 and p["chunk"] % 8 == 0
@@ -134,11 +134,11 @@ def test_plan_reductions():
     p = C.plan_reduce(C.variant("mean"), xt, torch.empty(100), [1], False)
     # rows adjacent and 16-byte aligned: lanes read 16 bytes of 4 rows (128 per group)
     assert (p["layout"], p["sa_row"], p["sa_in"], p["rg"]) == (1, 1, 100, 128)
-    assert p["flags"] & 2 and p["chunk"] == 64 and p["nseg"] == 47
-    assert p["nchunk"] == 47 and p["partials"] == 47 * 128 and p["counters"] == 1
+    assert p["flags"] & 2 and p["chunk"] == 128 and p["nseg"] == 24   # 64 KB chunks
+    assert p["nchunk"] == 24 and p["partials"] == 24 * 128 and p["counters"] == 1
     xb = torch.randn(3000, 256, dtype=torch.bfloat16).t()    # bf16: 8 rows per lane
     p = C.plan_reduce(C.variant("sum"), xb, torch.empty(256, dtype=torch.bfloat16), [1], False)
-    assert p["flags"] & 2 and p["rg"] == 256 and p["chunk"] == 64   # 32 KB chunks
+    assert p["flags"] & 2 and p["rg"] == 256 and p["chunk"] == 128   # 64 KB chunks
     xo = torch.randn(3000, 99).t()                              # 99 rows: not a multiple of 4
     p = C.plan_reduce(C.variant("mean"), xo, torch.empty(99), [1], False)
     assert (p["layout"], p["rg"]) == (1, 32) and not p["flags"] & 2
@@ -152,8 +152,8 @@ def test_plan_reductions():
     wq = torch.randn(8, 16, 32).permute(2, 0, 1)     # reduced dims 0 and 2 do not
     p = C.plan_reduce(C.variant("sum"), wq, torch.empty(8), [0, 2], False)
     assert p["layout"] == 2 and p["has_ext"] == 1 and p["inner"] == 32 * 16
-    # 512 reduced elements per output: a warp per output, 8192 / 512 outputs a chunk
-    assert p["rg"] == 1 and p["chunk"] == 16 and p["nchunk"] == 1
+    # 512 reduced elements per output: a warp per output, 16384 / 512 outputs a chunk
+    assert p["rg"] == 1 and p["chunk"] == 32 and p["nchunk"] == 1
     wr = torch.randn(8, 4, 6).permute(2, 0, 1)       # 24 per output: a lane per output
     p = C.plan_reduce(C.variant("sum"), wr, torch.empty(8), [0, 2], False)
     assert p["layout"] == 2 and p["rg"] == 0 and p["chunk"] == 32
