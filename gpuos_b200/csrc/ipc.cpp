@@ -297,7 +297,7 @@ struct gpuos_ipc_server {
       }
       clients.store(live, std::memory_order_relaxed);
       if (!marks.empty()) {
-        // one executor flush for every client that flushed this round
+        // one executor flush for every client that flushed in this pass
         h->client_flushes += marks.size();
         h->launch_flushes += 1;
         uint64_t ticket = 0;

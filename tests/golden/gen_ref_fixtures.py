@@ -168,7 +168,8 @@ def mixed_stream(ref, dev="cuda", reps=3):
 
 
 def main():
-    outdir = Path(sys.argv[1] if len(sys.argv) > 1 else "gpurun_out")
+    # default: this directory, where the committed fixtures live
+    outdir = Path(sys.argv[1]) if len(sys.argv) > 1 else Path(__file__).resolve().parent
     outdir.mkdir(parents=True, exist_ok=True)
     ref = RR.Reference()
     t0 = time.time()
