@@ -799,6 +799,12 @@ def bench_ours(args, world, rank, local):
     host_out = dout.cpu()  # the last timed step's outputs, checked below
     per_rank_ms = [round(v * 1e3, 3) for v in allgather(max(ev_s, wall) / args.steps, world)]
     t_step = max(per_rank_ms) / 1e3  # per step, slowest rank
+    # the share of each rank's timed region its batch kernels ran (their
+    # device time from the executor's %globaltimer stamps; -1: not available)
+    busy = -1.0
+    if "dev_ns" in q0 and "dev_ns" in q1 and max(ev_s, wall) > 0:
+        busy = (q1["dev_ns"] - q0["dev_ns"]) / 1e9 / max(ev_s, wall)
+    per_rank_busy = [round(v, 4) for v in allgather(busy, world)]
     torch.cuda.synchronize()
     clk = clocks.stop()
     batches = q1["tail"] - q0["tail"]
@@ -885,6 +891,7 @@ def bench_ours(args, world, rank, local):
                    "parallelism": f"{world} independent executors (one per GPU)"},
         "gbs_whole_step": round(world * stream.algo_bytes / t_step / 1e9, 1),
         "per_rank_ms_per_step": per_rank_ms,
+        "per_rank_gpu_busy": per_rank_busy,
         "e2e": {"value": round(world * n_req / t_e2e, 1), "unit": "requests/s",
                 "h2d_bytes_per_step": stream.in_bytes, "d2h_bytes_per_step": stream.out_bytes},
         "roofline": roof,
