@@ -259,3 +259,27 @@ def test_mixed_custom_and_precompiled_batch_is_one_launch(mode):
     assert torch.allclose(m.cpu().double(), M, rtol=1e-5, atol=1e-6)
     want = (H * torch.rsqrt(m.cpu() + 1e-6)) * w
     assert torch.allclose(o.cpu(), want, rtol=1e-5, atol=1e-6)
+
+
+def test_five_leaves_fall_back_to_a_partial_composition():
+    """(a*b + c) * (d - e): inlining both sides needs five leaves; the
+    left side is inlined and the right side's result becomes a leaf."""
+    ext = FakeExt()
+    m = _mode(ext)
+    a, b, c, d, e = (torch.randn(6) for _ in range(5))
+    ab = torch.empty(6)
+    m._node("bin|aten::mul.Tensor", "(A * B)", [a, b], ab)
+    l = torch.empty(6)
+    m._node("bin|aten::add.Tensor", "(A + B)", [ab, c], l)
+    r = torch.empty(6)
+    m._node("bin|aten::sub.Tensor", "(A - B)", [d, e], r)
+    out = torch.empty(6)
+    m._node("bin|aten::mul.Tensor", "(A * B)", [l, r], out)
+    del ab, l
+    m.submit_nodes()
+    calls = [(k, e_, [id(t) for t in ins], o) for k, e_, ins, o in ext.calls]
+    # r is written (a leaf of the result); the result inlines l's chain
+    assert [c_[0] for c_ in calls] == ["binary", "nary"]
+    assert calls[0][3] is r and calls[1][3] is out
+    assert calls[1][1] == "((gpuos_keep_f32(((gpuos_keep_f32((A * B))) + C))) * D)"
+    assert calls[1][2] == [id(a), id(b), id(c), id(r)]

@@ -179,3 +179,21 @@ def test_clients_share_one_executor():
         st = s.stats()
         assert st["requests"] == 3 * 4
         assert st["launch_flushes"] <= st["client_flushes"]
+
+
+def test_record_mode_four_input_requests_and_mailbox_limits():
+    name = _name("nary")
+    with I.Server(name, device=-1, pool_bytes=1 << 20, max_clients=2, ring_entries=4) as s:
+        with I.Client(name, timeout_s=10) as c:
+            ts = [_desc(c.base + 4096 * k, 256) for k in range(5)]
+            arr = (C.Tensor * 4)(*ts[:4])
+            for _ in range(6):                               # wraps the 4-entry ring
+                C.check(C.lib().gpuos_ipc_submit_slot(c.h, 3, 4, arr, ctypes.byref(ts[4])))
+            c.flush(sync=True)
+            assert s.stats()["requests"] == 6
+            with pytest.raises(C.GpuosError):                # five inputs: rejected
+                C.check(C.lib().gpuos_ipc_submit_slot(c.h, 3, 5, arr, ctypes.byref(ts[4])))
+            with pytest.raises(C.GpuosError) as e:           # longer than the mailbox holds
+                c.register_elementwise("k" * 300, "(A + B)", 2)
+            assert e.value.code == C.EINVAL
+            assert c.register_elementwise("ok", "(A + B)", 2) >= 0
